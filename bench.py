@@ -1,0 +1,409 @@
+"""Benchmark: NU points/s of the NUFFT execute path on B200 (one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C]
+                    [--impl reference]
+
+Workload (default --config 2, the configuration BASELINE.json's metric is
+quoted on): 1D type 2, N = 2^20 complex64 modes, M = 1e7 points uniform in
+[-pi, pi), eps = 1e-6, isign = -1.  A step is one plan execute over resident
+device inputs: pad/deconvolve -> cuFFT -> interp (setpts / sort excluded, the
+reference's "exec" protocol).  Each step is bracketed by CUDA events on the
+execute stream; L2 is flushed (256 MiB write) between steps, outside the
+events.  `value` = points of all ranks / max-over-ranks device time.
+
+Other keys: `roofline` (the dominant own kernel, from the plan's live stage
+events and the algorithmic bytes of the stage), `e2e` (same metric through
+the public API from pinned host memory with the H2D / D2H copies timed),
+`cpu_baseline` (the CPU oracle port on a bounded sample, rank 0),
+`gpu_launches` (own kernels launched in the timed region), `clocks`
+(nvidia-smi samples taken during the timed region).
+
+--impl reference times the CPU port of the reference algorithm
+(oracle/port.py; the reference itself has no CPU type-1/2 path and its Metal
+GPU path cannot run here) with all host threads, on rank 0 only.
+"""
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = ("NU points/sec per GPU (spread+FFT+deconv, device-timed) at "
+          "eps=1e-6; % HBM roofline")
+UNIT = "NU pts/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--scale", type=float, default=1.0,
+                    help="point-count scale (1.0 = the BASELINE size)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sms, maxs, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                 "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sms.append(float(parts[0]))
+                maxs.append(float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sms:
+            return None
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxs),
+                "samples": len(sms), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------- traffic
+def ncu_traffic(kernel_tag):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
+    summary (profiles/*.md line 'traffic_bytes_per_launch: <n>' under the
+    heading for this workload); None if absent."""
+    pdir = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(pdir):
+        return None
+    for f in sorted(os.listdir(pdir)):
+        if not f.endswith(".md") or kernel_tag not in f:
+            continue
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)",
+                      open(os.path.join(pdir, f)).read())
+        if m:
+            return float(m.group(1))
+    return None
+
+
+# ---------------------------------------------------------------- workload
+def algorithmic_bytes(cfg, info, stage):
+    """Compulsory DRAM bytes of one launch of the given stage's own kernel.
+    interp (type 2): per point cell (8 B/dim) + output (8 B) + permutation
+    (4 B, when sorted); grid read once (8 B/cell).  pad: modes read (8 B) +
+    grid written (8 B/cell).  spread (type 1): per point cell + strength
+    (8 B) + permutation; grid written once per vector."""
+    dim = info.dim
+    M = int(info.M)
+    ncell = int(np.prod([info.n_up[d] for d in range(dim)]))
+    K = int(np.prod([info.n_modes[d] for d in range(dim)]))
+    perm = 4 if info.tiled or info.nsub > 0 else 0
+    if stage == "interp":
+        return M * (8 * dim + 8 + perm) + ncell * 8
+    if stage == "pad":
+        return K * 8 + ncell * 8
+    if stage == "spread":
+        return M * (8 * dim + 8 + perm) + ncell * 8
+    raise ValueError(stage)
+
+
+def build_plan(cfg, torch):
+    import mlx_nufft_b200 as nb
+    if cfg["type"] == 2:
+        plan = nb.Type2PlanND(tuple(cfg["x"]), cfg["n_modes"], eps=cfg["eps"],
+                              isign=cfg["isign"])
+    elif cfg["type"] == 1:
+        plan = nb.Type1PlanND(tuple(cfg["x"]), cfg["n_modes"], eps=cfg["eps"],
+                              isign=cfg["isign"])
+    else:
+        plan = nb.Type3Plan(tuple(cfg["x"]), tuple(cfg["s"]), eps=cfg["eps"],
+                            isign=cfg["isign"])
+    return plan
+
+
+def cpu_baseline(cfg, threads):
+    """Time the CPU oracle port of the reference algorithm on a bounded
+    sample and extrapolate to the full workload: pad + FFT once on the full
+    grid, interp/spread on a sample of the points, scaled by M / sample."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import port
+    x = cfg["x"]
+    M = x[0].size
+    dim = len(x)
+    if cfg["type"] == 2:
+        f = np.asarray(cfg["data"], dtype=np.complex128)
+        N = f.shape
+        w, beta, nup = port.fine_grid_sizes(N, cfg["eps"])
+        # plan-time work (excluded, as in the reference's exec protocol)
+        decs = []
+        for d in range(dim):
+            k = np.arange(-(N[d] // 2), N[d] - N[d] // 2, dtype=np.float64)
+            decs.append(1.0 / port.kernel_ft(2.0 * np.pi * k / nup[d], beta, w))
+        t0 = time.perf_counter()
+        g = f.copy()
+        for d in range(dim):
+            g = g * decs[d].reshape((1,) * d + (-1,) + (1,) * (dim - d - 1))
+        H = np.zeros(nup, dtype=np.complex128)
+        H[np.ix_(*[port._band(N[d], nup[d]) for d in range(dim)])] = g
+        V = port._fft(H, cfg["isign"])
+        t_grid = time.perf_counter() - t0
+        sample = min(M, 2_000_000)
+        chunks = np.array_split(np.arange(sample), threads)
+
+        def work(ix):
+            i1s, frs = [], []
+            for d in range(dim):
+                i1, fr64, _ = port.cells_fold(x[d][ix], nup[d], w)
+                i1s.append(i1)
+                frs.append(fr64)
+            return port.interp(V, i1s, frs, w, beta, chunk=65536)
+
+        t1 = time.perf_counter()
+        with ThreadPoolExecutor(threads) as ex:
+            list(ex.map(work, chunks))
+        t_pts = time.perf_counter() - t1
+    else:
+        raise NotImplementedError("cpu baseline implemented for type-2 configs")
+    total = t_grid + t_pts * (M / sample)
+    return {"value": M / total, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": (f"oracle/port.py fp64: pad+FFT of the full grid "
+                       f"({t_grid:.2f} s) + interp of {sample} of {M} points "
+                       f"({t_pts:.2f} s), extrapolated to all points")}
+
+
+def run_reference(args):
+    """--impl reference: the CPU port, all host threads, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from mlx_nufft_b200 import gen
+    cfg = gen.config(args.config, scale=args.scale)
+    threads = os.cpu_count() or 1
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(cfg, threads)
+        if i >= args.warmup:
+            vals.append(r["value"])
+    v = float(np.median(vals))
+    r["value"] = v
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": cfg["x"][0].size / v * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f64", "data": "synthetic",
+            "config": {"workload": cfg["name"], "config": args.config},
+            "cpu_baseline": r,
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    from mlx_nufft_b200 import gen
+    # weak scaling: every rank owns its own point set (seed = rank)
+    cfg = gen.config(args.config, scale=args.scale, seed=rank)
+    plan = build_plan(cfg, torch)
+    native = plan._plan
+    info = native.info()
+    dev = torch.device("cuda", local)
+    data = torch.from_numpy(np.ascontiguousarray(
+        np.asarray(cfg["data"]).astype(np.complex64))).to(dev)
+    ndata = data.numel()
+    if cfg["type"] == 2:
+        n_out, nvec = int(info.M), 1
+        stage_own = "interp"
+    elif cfg["type"] == 1:
+        nvec = int(cfg.get("n_trans", 1))
+        n_out = int(np.prod(cfg["n_modes"])) * nvec
+        stage_own = "spread"
+    else:
+        n_out, nvec = int(info.N_tgt), 1
+        stage_own = "interp"
+    out = torch.empty(n_out, dtype=torch.complex64, device=dev)
+    flush = torch.empty(256 * 2 ** 20, dtype=torch.uint8, device=dev)
+    npts = int(info.M) * nvec
+
+    def step():
+        native.execute(data, out, nvec)
+
+    native.set_profile(True)
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    ev = [(torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    stage_ms = {"spread_or_pad": 0.0, "fft": 0.0, "interp_or_crop": 0.0}
+    barrier()
+    w0 = time.perf_counter()
+    for i in range(args.steps):
+        flush.zero_()
+        ev[i][0].record()
+        step()
+        ev[i][1].record()
+        st = native.stage_times()
+        for k in stage_ms:
+            stage_ms[k] += st[k]
+    barrier()
+    wall = time.perf_counter() - w0
+    clocks = sampler.stop()
+    native.set_profile(False)
+    dev_ms = sum(a.elapsed_time(b) for a, b in ev)
+    t = torch.tensor([dev_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    tmax_ms = float(t.item())
+    value = world * npts * args.steps / (tmax_ms / 1e3)
+
+    # ---- e2e through the public API, pinned host buffers -----------------
+    host_in = torch.from_numpy(np.ascontiguousarray(
+        np.asarray(cfg["data"]).astype(np.complex64))).pin_memory()
+    e2e_ms = []
+    for i in range(max(2, args.steps // 2) + 2):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        flush.zero_()
+        torch.cuda.synchronize()
+        a.record()
+        if cfg["type"] == 2:
+            res = plan.execute(host_in, return_np=True)
+        elif cfg["type"] == 1:
+            res = plan.execute_batch(host_in.reshape(nvec, -1), return_np=True) \
+                if nvec > 1 else plan.execute(host_in, return_np=True)
+        else:
+            res = plan.execute(host_in, return_np=True)
+        b.record()
+        torch.cuda.synchronize()
+        if i >= 2:
+            e2e_ms.append(a.elapsed_time(b))
+    e2e_t = torch.tensor([float(np.median(e2e_ms))], dtype=torch.float64,
+                         device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_val = world * npts / (float(e2e_t.item()) / 1e3)
+
+    # ---- roofline of the dominant own kernel ------------------------------
+    peak, peak_kind = peaks()
+    key = "interp_or_crop" if stage_own == "interp" else "spread_or_pad"
+    kern_ms = stage_ms[key] / args.steps
+    alg = algorithmic_bytes(cfg, info, stage_own)
+    achieved = alg / (kern_ms / 1e3) / 1e9
+    traffic = ncu_traffic(f"cfg{args.config}")
+
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and world == 1 and cfg["type"] == 2:
+            try:
+                cpu = cpu_baseline(cfg, 1)
+            except Exception as e:          # reported, never fatal
+                cpu = {"error": str(e)}
+        launches_per_step = 2 if cfg["type"] == 2 else (2 if cfg["type"] == 1 else 4)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": tmax_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": cfg["name"], "config": args.config,
+                       "points_per_rank": int(info.M), "vectors": nvec,
+                       "eps": cfg["eps"], "isign": cfg["isign"],
+                       "w": int(info.w),
+                       "n_up": [int(info.n_up[d]) for d in range(info.dim)],
+                       "tiled": bool(info.tiled),
+                       "l2": "flushed between steps (256 MiB write)",
+                       "wall_s_timed_region": wall},
+            "stage_ms": {k: v / args.steps for k, v in stage_ms.items()},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": traffic, "kernel": stage_own,
+                         "algorithmic_bytes": alg, "kernel_ms": kern_ms,
+                         "peak_kind": peak_kind},
+            "e2e": {"value": e2e_val, "unit": UNIT,
+                    "h2d_bytes_per_step": int(ndata * 8),
+                    "d2h_bytes_per_step": int(n_out * 8),
+                    "ms_per_step": float(e2e_t.item())},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    del plan, native
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,217 @@
+// deconv.cu -- fused mode-copy / deconvolution kernels and expi.
+//
+// crop (type 1, mlx_nufft/nd.py:416-435): FFT-ordered fine grid -> modeord=0
+//   mode box, times the per-dimension correction 1/phihat(2 pi k / n).
+// pad (type 2 nd.py:878-906, type 3 gpu_t3.py:629-651): mode box times the
+//   correction into the zero-padded FFT-ordered fine grid (zeros written too,
+//   so no separate memset pass).
+// Both run one CTA row per outer-index row of the output and sweep the
+// innermost (contiguous) dimension with consecutive threads, so every global
+// access is coalesced and index decomposition costs two integer divisions
+// per CTA rather than per element.  The outer-dimension correction factor
+// is formed once per row.
+//
+// expi (mlx_nufft/dfmath.py:29-134): the reference forms the phase in
+// double-single and reduces it mod 2 pi before fp32 cos/sin.  B200 has
+// native fp64, so the components are summed in fp64 and reduced with a
+// two-constant Cody-Waite step (2 pi = kTwoPi + kTwoPiLo, the product
+// k * kTwoPi taken exactly by fma); the O(1) residual is split into a float
+// pair and evaluated with sincosf plus a first-order correction for the low
+// part.
+#include <algorithm>
+
+#include "internal.h"
+
+namespace nufft {
+
+struct DecPtrs {
+    const float* d[3];
+};
+
+// Extents of a box and of the fine grid, innermost dimension last.
+struct BoxGrid {
+    int dim;
+    int N[3];      // mode box (1 for unused leading dims)
+    int n[3];      // fine grid
+    int64_t K;     // prod N
+    int64_t ncells;  // prod n
+};
+
+// Map an "outer" row index (all dims but the last) to per-dim indices.
+__device__ __forceinline__ void split_row(int64_t row, const int* ext, int dim,
+                                          int* idx) {
+    // dims 0 .. dim-2 are outer
+    for (int d = dim - 2; d >= 0; --d) {
+        idx[d] = (int)(row % ext[d]);
+        row /= ext[d];
+    }
+}
+
+// Type-1 crop: fk[v][m] = grid[v][r(m)] * prod_d dec_d[m_d], with
+// r_d = m_d - N_d/2 (+ n_d if negative).
+__global__ void __launch_bounds__(256)
+k_crop(const float2* __restrict__ grid, float2* __restrict__ fk, DecPtrs dec,
+       BoxGrid bg, int chunks_per_row) {
+    const int dim = bg.dim;
+    const int L = dim - 1;                    // innermost dim index
+    const int64_t row = blockIdx.x / chunks_per_row;
+    const int m_in = (int)(blockIdx.x % chunks_per_row) * blockDim.x + threadIdx.x;
+    if (m_in >= bg.N[L]) return;
+    const int v = blockIdx.y;
+    int m[3] = {0, 0, 0};
+    split_row(row, bg.N, dim, m);
+    int64_t rrow = 0;
+    float dout = 1.0f;
+    for (int d = 0; d < L; ++d) {
+        int r = m[d] - bg.N[d] / 2;
+        if (r < 0) r += bg.n[d];
+        rrow = rrow * bg.n[d] + r;
+        dout = (d == 0) ? dec.d[0][m[0]] : dout * dec.d[d][m[d]];
+    }
+    int r = m_in - bg.N[L] / 2;
+    if (r < 0) r += bg.n[L];
+    const float dd = (L == 0) ? dec.d[0][m_in] : dout * dec.d[L][m_in];
+    const float2 g = grid[v * bg.ncells + rrow * bg.n[L] + r];
+    fk[v * bg.K + row * bg.N[L] + m_in] = make_float2(g.x * dd, g.y * dd);
+}
+
+// Pad: H[v][r] = f[v][m(r)] * prod dec if every dim is in band, else 0.
+// In-band test (nd.py:894-901): q = r - n if r >= n - N/2; band is
+// -N/2 <= q < N - N/2; m = q + N/2.
+__global__ void __launch_bounds__(256)
+k_pad(const float2* __restrict__ f, float2* __restrict__ H, DecPtrs dec,
+      BoxGrid bg, int chunks_per_row) {
+    const int dim = bg.dim;
+    const int L = dim - 1;
+    const int64_t row = blockIdx.x / chunks_per_row;
+    const int r_in = (int)(blockIdx.x % chunks_per_row) * blockDim.x + threadIdx.x;
+    if (r_in >= bg.n[L]) return;
+    const int v = blockIdx.y;
+    int r[3] = {0, 0, 0};
+    split_row(row, bg.n, dim, r);
+    bool inband = true;
+    int64_t mrow = 0;
+    float dout = 1.0f;
+    for (int d = 0; d < L; ++d) {
+        int q = r[d];
+        if (q >= bg.n[d] - bg.N[d] / 2) q -= bg.n[d];
+        const int md = q + bg.N[d] / 2;
+        inband &= (md >= 0) && (md < bg.N[d]);
+        if (inband) {
+            mrow = mrow * bg.N[d] + md;
+            dout = (d == 0) ? dec.d[0][md] : dout * dec.d[d][md];
+        }
+    }
+    int q = r_in;
+    if (q >= bg.n[L] - bg.N[L] / 2) q -= bg.n[L];
+    const int mi = q + bg.N[L] / 2;
+    float2 out = make_float2(0.0f, 0.0f);
+    if (inband && mi >= 0 && mi < bg.N[L]) {
+        const float dd = (L == 0) ? dec.d[0][mi] : dout * dec.d[L][mi];
+        const float2 g = f[v * bg.K + mrow * bg.N[L] + mi];
+        out = make_float2(g.x * dd, g.y * dd);
+    }
+    H[v * bg.ncells + row * bg.n[L] + r_in] = out;
+}
+
+namespace {
+
+BoxGrid make_boxgrid(int dim, const int64_t* N, const int64_t* n) {
+    BoxGrid bg{};
+    bg.dim = dim;
+    bg.K = 1;
+    bg.ncells = 1;
+    for (int d = 0; d < 3; ++d) {
+        bg.N[d] = d < dim ? (int)N[d] : 1;
+        bg.n[d] = d < dim ? (int)n[d] : 1;
+    }
+    for (int d = 0; d < dim; ++d) {
+        bg.K *= N[d];
+        bg.ncells *= n[d];
+    }
+    return bg;
+}
+
+DecPtrs make_dec(const float* const* dec) {
+    DecPtrs dp{};
+    for (int d = 0; d < 3; ++d) dp.d[d] = dec[d];
+    return dp;
+}
+
+}  // namespace
+
+void launch_crop(int dim, const int64_t* N, const int64_t* n,
+                 const float* const* dec, const float2* grid, float2* fk,
+                 int nvec, cudaStream_t st) {
+    const BoxGrid bg = make_boxgrid(dim, N, n);
+    const int inner = bg.N[dim - 1];
+    const int cpr = (inner + 255) / 256;
+    const int64_t rows = bg.K / inner;
+    const int64_t blocks = rows * cpr;
+    if (blocks > 0x7fffffffLL) fail(-1, "mode box too large");
+    for (int v0 = 0; v0 < nvec; v0 += 65535) {
+        const int nv = std::min(65535, nvec - v0);
+        dim3 g((unsigned)blocks, (unsigned)nv);
+        k_crop<<<g, 256, 0, st>>>(grid + v0 * bg.ncells, fk + v0 * bg.K,
+                                  make_dec(dec), bg, cpr);
+        NUFFT_LAUNCH("k_crop");
+    }
+}
+
+void launch_pad(int dim, const int64_t* N, const int64_t* n,
+                const float* const* dec, const float2* f, float2* H, int nvec,
+                cudaStream_t st) {
+    const BoxGrid bg = make_boxgrid(dim, N, n);
+    const int inner = bg.n[dim - 1];
+    const int cpr = (inner + 255) / 256;
+    const int64_t rows = bg.ncells / inner;
+    const int64_t blocks = rows * cpr;
+    if (blocks > 0x7fffffffLL) fail(-1, "fine grid too large");
+    for (int v0 = 0; v0 < nvec; v0 += 65535) {
+        const int nv = std::min(65535, nvec - v0);
+        dim3 g((unsigned)blocks, (unsigned)nv);
+        k_pad<<<g, 256, 0, st>>>(f + v0 * bg.K, H + v0 * bg.ncells,
+                                 make_dec(dec), bg, cpr);
+        NUFFT_LAUNCH("k_pad");
+    }
+}
+
+// ---------------------------------------------------------------------
+constexpr int kMaxExpiComps = 64;
+struct ExpiComps {
+    const double* p[kMaxExpiComps];
+};
+
+__global__ void __launch_bounds__(256)
+k_expi(ExpiComps comps, int ncomp, int64_t n, float sgn,
+       float2* __restrict__ out) {
+    const int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    double phi = 0.0;
+    for (int c = 0; c < ncomp; ++c) phi += __ldg(comps.p[c] + j);
+    const double k = rint(phi * (1.0 / kTwoPi));
+    double r = fma(-k, kTwoPi, phi);
+    r = fma(-k, kTwoPiLo, r);
+    const float hi = (float)r;
+    const float lo = (float)(r - (double)hi);
+    float s, c;
+    sincosf(hi, &s, &c);
+    const float sr = fmaf(c, lo, s);     // sin(hi + lo) to first order
+    const float cr = fmaf(-s, lo, c);    // cos(hi + lo) to first order
+    out[j] = make_float2(cr, sgn * sr);
+}
+
+void launch_expi(int ncomp, const double* const* comps, int64_t n, int isign,
+                 float2* out, cudaStream_t st) {
+    if (ncomp < 1 || ncomp > kMaxExpiComps)
+        fail(-1, "expi: between 1 and 64 phase components are supported");
+    if (n <= 0) return;
+    ExpiComps cp{};
+    for (int c = 0; c < ncomp; ++c) cp.p[c] = comps[c];
+    const int64_t blocks = (n + 255) / 256;
+    k_expi<<<(unsigned)blocks, 256, 0, st>>>(cp, ncomp, n,
+                                             isign >= 0 ? 1.0f : -1.0f, out);
+    NUFFT_LAUNCH("k_expi");
+}
+
+}  // namespace nufft

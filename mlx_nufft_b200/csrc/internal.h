@@ -1,0 +1,161 @@
+// internal.h -- declarations shared by the translation units of
+// libnufft_b200.so.  Not part of the public C ABI (include/nufft_b200.h).
+#pragma once
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+namespace nufft {
+
+constexpr double kPi = 3.141592653589793238462643383279502884;
+// 2*pi as the nearest double (== 2.0 * numpy.pi) and the remainder, used
+// for the Cody-Waite reduction mod 2*pi (Cody & Waite, "Software Manual
+// for the Elementary Functions", 1980).
+constexpr double kTwoPi = 6.283185307179586;
+constexpr double kTwoPiLo = 2.4492935982947064e-16;
+
+// ---------------------------------------------------------------------
+// errors: every C-ABI entry converts a thrown Error into a status code.
+struct Error {
+    int code;
+    std::string msg;
+};
+[[noreturn]] void fail(int code, const std::string& msg);
+void check_cuda(cudaError_t e, const char* what);
+void set_last_error(const std::string& msg);
+
+#define NUFFT_CUDA(call) ::nufft::check_cuda((call), #call)
+#define NUFFT_LAUNCH(what) ::nufft::check_cuda(cudaGetLastError(), what)
+
+// ---------------------------------------------------------------------
+// host numerics (sizing.cpp) -- restatements of mlx_nufft/sizing.py
+int64_t next235even(int64_t n);
+void kernel_params(double eps, double upsampfac, int* w, double* beta);
+// 128-node Gauss-Legendre nodes d_q on [0, w/2] and weights a_q =
+// wq_q * psi(d_q) such that phihat(xi) = 2 * sum_q a_q cos(xi d_q).
+void kernel_ft_nodes(double beta, int w, std::vector<double>* d,
+                     std::vector<double>* a);
+double kernel_ft(double xi, double beta, int w);
+void set_nhg_type3(double S, double X, double upsampfac, int w, int64_t* nf,
+                   double* h, double* gam);
+
+// ---------------------------------------------------------------------
+// geometry handed to the device kernels by value.
+
+// How one nonuniform coordinate becomes (cell index i1, fraction fr).
+enum CellKind : int {
+    CELL_FOLD = 0,    // types 1/2: xi = mod(x, 2pi) / h           (nd.py:152-165)
+    CELL_T3SRC = 1,   // type-3 sources: ((x - C)/gam)/h + nf/2     (gpu_t3.py:486-490)
+    CELL_T3TGT = 2,   // type-3 targets: (s - D)*(h*gam)/h2 + n/2   (gpu_t3.py:357-366)
+};
+
+struct CellParams {
+    int kind;             // CellKind
+    int dim;
+    int fp32;             // 1: rescale in fp32 (prec "fp32" / "phases64")
+    int halfw;            // w / 2 (integer division), bin offset
+    double halfw_d;       // w / 2.0
+    int64_t n[3];         // grid extent the cells live on
+    double h[3];          // CELL_FOLD: 2pi/n ; CELL_T3SRC: 2pi/nf
+    double a[3];          // CELL_T3SRC: C ; CELL_T3TGT: D
+    double b[3];          // CELL_T3SRC: gam ; CELL_T3TGT: h*gam (python double)
+    double c[3];          // CELL_T3SRC: nf/2.0 ; CELL_T3TGT: 2pi/n_up
+    double e[3];          // CELL_T3TGT: n_up/2.0
+    int m[3];             // bin extent
+    int nb[3];            // bins per dimension
+};
+
+struct TileGeom {
+    int dim;
+    int n[3];             // grid extent (unused dims 1)
+    int64_t ncells;       // prod n
+    int m[3];             // bin extent
+    int nb[3];            // bins per dimension
+    int T[3];             // tile extent m + w - 1 (unused dims 1)
+    int tcells;           // prod T
+    int halfw;            // w / 2
+    float c2w;            // (float)(2.0 / w)
+    float beta;           // (float) beta
+};
+
+// One sorted (or caller-ordered) set of nonuniform points on the device.
+struct PointSet {
+    int dim = 0;
+    int64_t M = 0;
+    int2* cell[3] = {nullptr, nullptr, nullptr};  // (i1, fr bits) per point
+    uint32_t* perm = nullptr;   // sorted position -> caller index (null: identity)
+    int4* subs = nullptr;       // (start, count, bin, 0) per subproblem
+    int64_t nsub = 0;
+    int64_t cap = 0;            // allocated points
+    int64_t subcap = 0;         // allocated subproblems
+    float2* phase = nullptr;    // type 3: prephase / postphase, sorted order
+    bool sorted = false;
+    bool tiled = false;
+};
+
+// ---------------------------------------------------------------------
+// device memory helpers
+void* dmalloc(size_t bytes, const char* what);
+void dfree(void* p);
+
+// ---------------------------------------------------------------------
+// points.cu
+// Count + scan + scatter bin sort (or plain caller-order cells when
+// sort == false) of M points with coordinates coords[0..dim).
+// `phase_mode`: 0 none, 1 type-3 prephase (sources), 2 type-3 post (targets).
+struct PhaseParams {
+    int mode;            // 0 none, 1 prephase, 2 post
+    int isign;
+    int fp32;            // phases computed in fp32 (prec fp32 / coords64)
+    double D[3];         // prephase: e^{i isign sum D_d x_d}
+    double C[3];         // post: e^{i isign sum C_d (s_d - D_d)} / prod phihat
+    const double* ftd;   // device: 128 quadrature nodes d_q (post)
+    const double* fta;   // device: 128 weights a_q (post)
+    int nq;
+};
+void build_pointset(PointSet* ps, const CellParams& cp, int64_t M,
+                    const double* const* coords, bool sort, bool tiled,
+                    int msub, const PhaseParams& pp, int* d_err,
+                    cudaStream_t st);
+void free_pointset(PointSet* ps);
+// min/max of `n` device arrays of length M each; out: 2*n doubles (min,max)
+void device_minmax(int n, const double* const* arrs, int64_t M, double* out,
+                   cudaStream_t st);
+
+// spreadinterp.cu
+// Spread nvec strength vectors (c, vector stride cstride) onto nvec fine
+// grids (grid stride = tg.ncells), accumulating (grid must be zeroed).
+void launch_spread(const PointSet& ps, const TileGeom& tg, int w,
+                   const float2* c, int64_t cstride, int nvec,
+                   float2* grid, int nvg, cudaStream_t st);
+// Interpolate nvec grids at the points into out (vector stride ostride),
+// multiplying by ps.phase when present.
+void launch_interp(const PointSet& ps, const TileGeom& tg, int w,
+                   const float2* grid, int nvec, float2* out, int64_t ostride,
+                   int nvg, cudaStream_t st);
+// Largest dynamic shared memory a tile kernel may use (bytes).
+int tile_smem_limit();
+// Spread one group of a disjoint-support batch: point j goes to grid
+// groups[perm[j]] only (global-memory atomics).
+void launch_spread_groups(const PointSet& ps, const TileGeom& tg, int w,
+                          const float2* c, const int32_t* groups,
+                          float2* grid, cudaStream_t st);
+
+// deconv.cu
+// Type-1 crop: fk[v][m] = grid[v][r(m)] * prod dec_d[m_d]   (nd.py:416-435)
+void launch_crop(int dim, const int64_t* N, const int64_t* n,
+                 const float* const* dec, const float2* grid, float2* fk,
+                 int nvec, cudaStream_t st);
+// Pad: H[v][r] = in-band ? f[v][m(r)] * prod dec_d[m_d] : 0
+// (types 2 and 3: nd.py:878-906, gpu_t3.py:629-651)
+void launch_pad(int dim, const int64_t* N, const int64_t* n,
+                const float* const* dec, const float2* f, float2* H,
+                int nvec, cudaStream_t st);
+// e^{i isign sum_c comps[c][j]}  (dfmath.py:29-54)
+void launch_expi(int ncomp, const double* const* comps, int64_t n, int isign,
+                 float2* out, cudaStream_t st);
+
+}  // namespace nufft

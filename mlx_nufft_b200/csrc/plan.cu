@@ -1,0 +1,992 @@
+// plan.cu -- plan objects and the extern "C" entry points of libnufft_b200.
+//
+// A plan owns every device buffer the transform needs (sorted point cells,
+// permutation, subproblem tables, deconvolution vectors, fine grids, cuFFT
+// plans) and runs each execute asynchronously on the caller's stream with
+// no host synchronisation.  Stage structure follows the reference:
+//   type 1  zero grid -> spread -> FFT -> crop/deconvolve  (nd.py:581-625)
+//   type 2  pad/deconvolve -> FFT -> interp                (nd.py:1075-1119)
+//   type 3  zero -> prephase+spread (nf grid) -> pad/deconvolve to n_up ->
+//           FFT -> interp x post                          (gpu_t3.py:1287-1349)
+// cuFFT's inverse transform is unnormalised, so unlike the reference (whose
+// MLX ifft divides by n and is undone by folding prod(n_up) into dec[0],
+// nd.py:146-147, gpu_t3.py:388-392) no scale is folded into the corrections.
+#include <cufft.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/nufft_b200.h"
+#include "internal.h"
+
+namespace nufft {
+
+// ---------------------------------------------------------------------
+// errors
+thread_local std::string g_last_error;
+
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+
+void fail(int code, const std::string& msg) { throw Error{code, msg}; }
+
+void check_cuda(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return;
+    const int code = (e == cudaErrorMemoryAllocation) ? NUFFT_ERR_OOM : NUFFT_ERR_CUDA;
+    cudaGetLastError();  // clear a non-sticky error
+    fail(code, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+static void check_cufft(cufftResult r, const char* what) {
+    if (r == CUFFT_SUCCESS) return;
+    const int code = (r == CUFFT_ALLOC_FAILED) ? NUFFT_ERR_OOM : NUFFT_ERR_CUFFT;
+    fail(code, std::string(what) + ": cuFFT error " + std::to_string((int)r));
+}
+
+void* dmalloc(size_t bytes, const char* what) {
+    void* p = nullptr;
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        fail(e == cudaErrorMemoryAllocation ? NUFFT_ERR_OOM : NUFFT_ERR_CUDA,
+             std::string("device allocation of ") + std::to_string(bytes) +
+                 " bytes for " + what + " failed: " + cudaGetErrorString(e));
+    }
+    return p;
+}
+
+void dfree(void* p) {
+    if (p) cudaFree(p);
+}
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        NUFFT_CUDA(cudaGetDevice(&prev));
+        if (prev != dev) NUFFT_CUDA(cudaSetDevice(dev));
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (cudaGetDevice(&cur) == cudaSuccess && cur != prev && prev >= 0)
+            cudaSetDevice(prev);
+    }
+};
+
+template <typename F>
+int guarded(F&& f) {
+    try {
+        f();
+        return NUFFT_OK;
+    } catch (const Error& e) {
+        set_last_error(e.msg);
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        set_last_error("host allocation failed");
+        return NUFFT_ERR_OOM;
+    } catch (const std::exception& e) {
+        set_last_error(e.what());
+        return NUFFT_ERR_UNSUPPORTED;
+    }
+}
+
+std::mutex g_plan_mutex;   // serialises plan creation / cuFFT planning
+
+constexpr int kMsubSpread = 1024;   // points per spreading subproblem
+constexpr int kMsubInterp = 8192;   // points per interpolation subproblem
+constexpr int64_t kTiledMinPoints = 20000;  // below: global kernels (nd.py:304)
+constexpr size_t kTileBudget = 96 * 1024;   // smem per CTA for vector groups
+
+}  // namespace
+}  // namespace nufft
+
+using namespace nufft;
+
+struct nufft_plan_s {
+    int type = 0, dim = 0, device = 0, n_trans = 1, isign = 1;
+    double eps = 1e-6;
+    nufft_opts opts{};
+    double sigma = 2.0, sigma_in = 2.0;
+    int w = 0, w2 = 0;
+    double beta = 0, beta2 = 0;
+    int64_t N[3] = {1, 1, 1};
+    int64_t nf[3] = {1, 1, 1};     // spread grid (types 1/2: == nup)
+    int64_t nup[3] = {1, 1, 1};    // FFT grid
+    int64_t nfcells = 1, nupcells = 1, K = 1;
+    int nbatch = 1;
+    // type 3
+    double C[3] = {0, 0, 0}, D[3] = {0, 0, 0}, gam[3] = {1, 1, 1},
+           hf[3] = {0, 0, 0};
+    double xlo[3] = {0, 0, 0}, xhi[3] = {0, 0, 0};
+    bool sized = false;
+    bool points_set = false;
+    int64_t Ntgt = 0;
+    double* d_ftd = nullptr;   // quadrature nodes for phihat(beta, w)
+    double* d_fta = nullptr;
+    float* dec[3] = {nullptr, nullptr, nullptr};
+    PointSet src, tgt;
+    TileGeom tg_src{}, tg_tgt{};
+    int nvg_src = 1, nvg_tgt = 1;
+    float2* gspread = nullptr;   // type 3 only (nf grids)
+    float2* gfft = nullptr;      // n_up grids (types 1/2: also the spread grid)
+    std::map<int, cufftHandle> ffts;
+    bool profile = false;
+    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    bool ev_recorded = false;
+    int* d_err = nullptr;
+};
+
+namespace nufft_impl {
+
+// ----------------------------------------------------------------------
+// tiling choice per grid: bin extent m per dimension so that the tile
+// (m + w - 1)^dim of complex64 fits shared memory with room for several
+// vectors.
+TileGeom make_tile(int dim, const int64_t* n, int w, double beta) {
+    TileGeom tg{};
+    tg.dim = dim;
+    tg.ncells = 1;
+    tg.tcells = 1;
+    tg.halfw = w / 2;
+    tg.c2w = (float)(2.0 / w);
+    tg.beta = (float)beta;
+    int m0 = dim == 1 ? 1024 : (dim == 2 ? 32 : 8);
+    for (int d = 0; d < 3; ++d) {
+        if (d < dim) {
+            tg.n[d] = (int)n[d];
+            tg.m[d] = (int)std::min<int64_t>(m0, n[d]);
+            tg.nb[d] = (int)((n[d] + tg.m[d] - 1) / tg.m[d]);
+            tg.T[d] = tg.m[d] + w - 1;
+        } else {
+            tg.n[d] = tg.m[d] = tg.nb[d] = tg.T[d] = 1;
+        }
+    }
+    for (int d = 0; d < dim; ++d) {
+        tg.ncells *= n[d];
+        tg.tcells *= tg.T[d];
+    }
+    return tg;
+}
+
+bool tile_fits(const TileGeom& tg) {
+    return (size_t)tg.tcells * sizeof(float2) <= (size_t)tile_smem_limit();
+}
+
+int vectors_per_tile(const TileGeom& tg, int nbatch) {
+    const size_t per = (size_t)tg.tcells * sizeof(float2);
+    int nvg = (int)std::max<size_t>(1, kTileBudget / per);
+    if ((size_t)nvg * per > (size_t)tile_smem_limit())
+        nvg = (int)std::max<size_t>(1, tile_smem_limit() / per);
+    return std::max(1, std::min(nvg, nbatch));
+}
+
+bool want_tiled(const nufft_plan_s* p, int64_t npts, const TileGeom& tg) {
+    if (p->opts.method == NUFFT_METHOD_GLOBAL) return false;
+    const bool fits = tile_fits(tg);
+    if (p->opts.method == NUFFT_METHOD_TILED) {
+        if (!fits) fail(NUFFT_ERR_ARG, "tiled method not applicable: tile exceeds shared memory");
+        return true;
+    }
+    return fits && npts >= kTiledMinPoints;
+}
+
+void upload_dec(nufft_plan_s* p, int d, const std::vector<double>& v) {
+    std::vector<float> f(v.size());
+    for (size_t i = 0; i < v.size(); ++i) f[i] = (float)v[i];
+    dfree(p->dec[d]);
+    p->dec[d] = nullptr;
+    p->dec[d] = (float*)dmalloc(sizeof(float) * std::max<size_t>(f.size(), 1), "deconvolution");
+    NUFFT_CUDA(cudaMemcpy(p->dec[d], f.data(), sizeof(float) * f.size(),
+                          cudaMemcpyHostToDevice));
+}
+
+double phihat_host(double xi, const std::vector<double>& dq,
+                   const std::vector<double>& aq) {
+    double s = 0.0;
+    for (size_t q = 0; q < dq.size(); ++q) s += aq[q] * std::cos(xi * dq[q]);
+    return 2.0 * s;
+}
+
+void destroy_ffts(nufft_plan_s* p) {
+    for (auto& kv : p->ffts) cufftDestroy(kv.second);
+    p->ffts.clear();
+}
+
+cufftHandle get_fft(nufft_plan_s* p, int nv) {
+    auto it = p->ffts.find(nv);
+    if (it != p->ffts.end()) return it->second;
+    std::lock_guard<std::mutex> lk(g_plan_mutex);
+    cufftHandle h;
+    check_cufft(cufftCreate(&h), "cufftCreate");
+    long long n[3];
+    for (int d = 0; d < p->dim; ++d) n[d] = p->nup[d];
+    size_t ws = 0;
+    cufftResult r = cufftMakePlanMany64(h, p->dim, n, nullptr, 1, p->nupcells,
+                                        nullptr, 1, p->nupcells, CUFFT_C2C, nv,
+                                        &ws);
+    if (r != CUFFT_SUCCESS) {
+        cufftDestroy(h);
+        check_cufft(r, "cufftMakePlanMany64");
+    }
+    p->ffts[nv] = h;
+    return h;
+}
+
+void run_fft(nufft_plan_s* p, float2* grid, int nv, cudaStream_t st) {
+    cufftHandle h = get_fft(p, nv);
+    check_cufft(cufftSetStream(h, st), "cufftSetStream");
+    const int dir = p->isign > 0 ? CUFFT_INVERSE : CUFFT_FORWARD;
+    check_cufft(cufftExecC2C(h, (cufftComplex*)grid, (cufftComplex*)grid, dir),
+                "cufftExecC2C");
+}
+
+void alloc_grids(nufft_plan_s* p) {
+    dfree(p->gfft);
+    p->gfft = nullptr;
+    dfree(p->gspread);
+    p->gspread = nullptr;
+    p->gfft = (float2*)dmalloc(sizeof(float2) * p->nupcells * p->nbatch, "fine grid");
+    if (p->type == 3)
+        p->gspread = (float2*)dmalloc(sizeof(float2) * p->nfcells * p->nbatch,
+                                      "type-3 spread grid");
+}
+
+void record(nufft_plan_s* p, int i, cudaStream_t st) {
+    if (p->profile) NUFFT_CUDA(cudaEventRecord(p->ev[i], st));
+}
+
+void check_err_flag(nufft_plan_s* p, cudaStream_t st) {
+    int h = 0;
+    NUFFT_CUDA(cudaMemcpyAsync(&h, p->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    NUFFT_CUDA(cudaStreamSynchronize(st));
+    if (h) {
+        NUFFT_CUDA(cudaMemsetAsync(p->d_err, 0, sizeof(int), st));
+        NUFFT_CUDA(cudaStreamSynchronize(st));
+        fail(NUFFT_ERR_ARG, "non-finite nonuniform coordinate");
+    }
+}
+
+// ---------------------------------------------------------------------
+// types 1 / 2
+void create_t12(nufft_plan_s* p) {
+    p->sigma = p->opts.upsampfac > 0 ? p->opts.upsampfac : 2.0;
+    if (!(p->sigma > 1.0 && p->sigma <= 4.0))
+        fail(NUFFT_ERR_ARG, "upsampfac must be in (1, 4]");
+    kernel_params(p->eps, p->sigma, &p->w, &p->beta);
+    p->w2 = p->w;
+    p->beta2 = p->beta;
+    p->K = 1;
+    p->nupcells = 1;
+    for (int d = 0; d < p->dim; ++d) {
+        if (p->N[d] < 1) fail(NUFFT_ERR_ARG, "mode dims must be >= 1");
+        const int64_t up = (int64_t)std::ceil(p->sigma * (double)p->N[d]);
+        p->nup[d] = next235even(std::max<int64_t>(2 * p->w, up));
+        if (p->nup[d] > 0x7fffffffLL) fail(NUFFT_ERR_ARG, "fine grid too large");
+        p->nf[d] = p->nup[d];
+        p->K *= p->N[d];
+        p->nupcells *= p->nup[d];
+    }
+    p->nfcells = p->nupcells;
+    // corrections 1/phihat(2 pi k / n_up), k in [-N/2, N - N/2)  (nd.py:140-145)
+    std::vector<double> dq, aq;
+    kernel_ft_nodes(p->beta, p->w, &dq, &aq);
+    for (int d = 0; d < p->dim; ++d) {
+        std::vector<double> v(p->N[d]);
+        for (int64_t i = 0; i < p->N[d]; ++i) {
+            const double k = (double)(i - p->N[d] / 2);
+            v[i] = 1.0 / phihat_host(2.0 * kPi * k / (double)p->nup[d], dq, aq);
+        }
+        upload_dec(p, d, v);
+    }
+    p->tg_src = make_tile(p->dim, p->nup, p->w, p->beta);
+    p->nvg_src = vectors_per_tile(p->tg_src, p->nbatch);
+    alloc_grids(p);
+    p->sized = true;
+}
+
+void setpts_t12(nufft_plan_s* p, int64_t M, const double* const* xs,
+                cudaStream_t st) {
+    CellParams cp{};
+    cp.kind = CELL_FOLD;
+    cp.dim = p->dim;
+    cp.fp32 = p->opts.prec == NUFFT_PREC_FP32;
+    cp.halfw = p->w / 2;
+    cp.halfw_d = p->w / 2.0;
+    for (int d = 0; d < p->dim; ++d) {
+        cp.n[d] = p->nup[d];
+        cp.h[d] = 2.0 * kPi / (double)p->nup[d];
+        cp.m[d] = p->tg_src.m[d];
+        cp.nb[d] = p->tg_src.nb[d];
+    }
+    const bool tiled = want_tiled(p, M, p->tg_src);
+    const bool sort = tiled || p->opts.sort_points;
+    PhaseParams pp{};
+    build_pointset(&p->src, cp, M, xs, sort, tiled,
+                   p->type == 1 ? kMsubSpread : kMsubInterp, pp, p->d_err, st);
+    check_err_flag(p, st);
+    p->points_set = true;
+}
+
+// ---------------------------------------------------------------------
+// type 3
+void create_t3(nufft_plan_s* p) {
+    p->sigma = p->opts.upsampfac > 0 ? p->opts.upsampfac : 1.25;
+    if (!(p->sigma > 1.0)) fail(NUFFT_ERR_ARG, "upsampfac must be > 1");
+    kernel_params(p->eps, p->sigma, &p->w, &p->beta);
+    const double si = p->opts.sigma_inner;
+    if (si <= 0.0 || si == p->sigma) {
+        p->sigma_in = p->sigma;
+        p->w2 = p->w;
+        p->beta2 = p->beta;
+    } else {
+        if (!(si > 1.0)) fail(NUFFT_ERR_ARG, "sigma_inner must be > 1");
+        // gpu_t3.py:279-284
+        p->sigma_in = si;
+        int ns = (int)std::ceil(-std::log(p->eps) / (kPi * std::sqrt(1.0 - 1.0 / si)));
+        ns = std::max(2, std::min(ns, 16));
+        p->w2 = ns;
+        p->beta2 = 0.97 * kPi * (1.0 - 1.0 / (2.0 * si)) * ns;
+    }
+    std::vector<double> dq, aq;
+    kernel_ft_nodes(p->beta, p->w, &dq, &aq);
+    p->d_ftd = (double*)dmalloc(sizeof(double) * dq.size(), "phihat nodes");
+    p->d_fta = (double*)dmalloc(sizeof(double) * aq.size(), "phihat weights");
+    NUFFT_CUDA(cudaMemcpy(p->d_ftd, dq.data(), sizeof(double) * dq.size(),
+                          cudaMemcpyHostToDevice));
+    NUFFT_CUDA(cudaMemcpy(p->d_fta, aq.data(), sizeof(double) * aq.size(),
+                          cudaMemcpyHostToDevice));
+}
+
+// Size grids from source extents [xlo, xhi] and target extents [slo, shi]
+// (gpu_t3.py:322-342, 379-383).
+void size_t3(nufft_plan_s* p, const double* slo, const double* shi) {
+    int64_t nf_new[3], nup_new[3];
+    for (int d = 0; d < p->dim; ++d) {
+        p->C[d] = 0.5 * (p->xlo[d] + p->xhi[d]);
+        p->D[d] = 0.5 * (slo[d] + shi[d]);
+        const double X = 0.5 * (p->xhi[d] - p->xlo[d]);
+        const double S = 0.5 * (shi[d] - slo[d]);
+        double h;
+        set_nhg_type3(S, X, p->sigma, p->w, &nf_new[d], &h, &p->gam[d]);
+        p->hf[d] = 2.0 * kPi / (double)nf_new[d];
+        nup_new[d] = next235even((int64_t)std::ceil(p->sigma_in * (double)nf_new[d]));
+        if (nup_new[d] > 0x7fffffffLL) fail(NUFFT_ERR_ARG, "type-3 grid too large");
+    }
+    bool changed = !p->sized;
+    for (int d = 0; d < p->dim; ++d)
+        changed |= (nf_new[d] != p->nf[d]) || (nup_new[d] != p->nup[d]);
+    p->nfcells = p->nupcells = 1;
+    for (int d = 0; d < p->dim; ++d) {
+        p->nf[d] = nf_new[d];
+        p->nup[d] = nup_new[d];
+        p->nfcells *= p->nf[d];
+        p->nupcells *= p->nup[d];
+    }
+    // mode corrections (-1)^q / phihat2(2 pi q / n_up), q in [-nf/2, nf/2)
+    std::vector<double> dq, aq;
+    kernel_ft_nodes(p->beta2, p->w2, &dq, &aq);
+    for (int d = 0; d < p->dim; ++d) {
+        std::vector<double> v(p->nf[d]);
+        for (int64_t i = 0; i < p->nf[d]; ++i) {
+            const int64_t q = i - p->nf[d] / 2;
+            const double sgn = (q % 2 == 0) ? 1.0 : -1.0;
+            v[i] = sgn / phihat_host(2.0 * kPi * (double)q / (double)p->nup[d], dq, aq);
+        }
+        upload_dec(p, d, v);
+    }
+    if (changed) {
+        destroy_ffts(p);
+        alloc_grids(p);
+    }
+    p->tg_src = make_tile(p->dim, p->nf, p->w, p->beta);
+    p->nvg_src = vectors_per_tile(p->tg_src, p->nbatch);
+    p->tg_tgt = make_tile(p->dim, p->nup, p->w2, p->beta2);
+    p->nvg_tgt = vectors_per_tile(p->tg_tgt, p->nbatch);
+    p->sized = true;
+}
+
+void set_sources_t3(nufft_plan_s* p, int64_t M, const double* const* xs,
+                    bool check_guard, cudaStream_t st) {
+    if (check_guard) {
+        double mm[6];
+        device_minmax(p->dim, xs, M, mm, st);
+        for (int d = 0; d < p->dim; ++d) {
+            const double guard = 0.45 * (p->w + 1) * p->gam[d] * (2.0 * kPi / (double)p->nf[d]);
+            if (mm[2 * d] < p->xlo[d] - guard || mm[2 * d + 1] > p->xhi[d] + guard) {
+                char buf[256];
+                snprintf(buf, sizeof buf,
+                         "set_sources: dim %d sources exceed the frozen plan extent "
+                         "[%.4g, %.4g] (+guard %.3g); rebuild the plan for this geometry",
+                         d, p->xlo[d], p->xhi[d], guard);
+                fail(NUFFT_ERR_RANGE, buf);
+            }
+        }
+    }
+    CellParams cp{};
+    cp.kind = CELL_T3SRC;
+    cp.dim = p->dim;
+    const int prec = p->opts.prec;
+    cp.fp32 = !(prec == NUFFT_PREC_CRIT64 || prec == NUFFT_PREC_COORDS64);
+    cp.halfw = p->w / 2;
+    cp.halfw_d = p->w / 2.0;
+    for (int d = 0; d < p->dim; ++d) {
+        cp.n[d] = p->nf[d];
+        cp.a[d] = p->C[d];
+        cp.b[d] = p->gam[d];
+        cp.h[d] = p->hf[d];
+        cp.c[d] = p->nf[d] / 2.0;
+        cp.m[d] = p->tg_src.m[d];
+        cp.nb[d] = p->tg_src.nb[d];
+    }
+    PhaseParams pp{};
+    pp.mode = 1;
+    pp.isign = p->isign;
+    pp.fp32 = !(prec == NUFFT_PREC_CRIT64 || prec == NUFFT_PREC_PHASES64);
+    for (int d = 0; d < p->dim; ++d) pp.D[d] = p->D[d];
+    const bool tiled = want_tiled(p, M, p->tg_src);
+    const bool sort = tiled || p->opts.sort_points;
+    build_pointset(&p->src, cp, M, xs, sort, tiled, kMsubSpread, pp, p->d_err, st);
+    check_err_flag(p, st);
+}
+
+void setpts_t3(nufft_plan_s* p, int64_t M, const double* const* xs, int64_t N,
+               const double* const* ss, cudaStream_t st) {
+    if (N < 1) fail(NUFFT_ERR_ARG, "at least one target is required");
+    double smm[6], xmm[6];
+    device_minmax(p->dim, ss, N, smm, st);
+    if (p->opts.has_source_extent) {
+        for (int d = 0; d < p->dim; ++d) {
+            p->xlo[d] = p->opts.source_extent[2 * d];
+            p->xhi[d] = p->opts.source_extent[2 * d + 1];
+        }
+    } else {
+        device_minmax(p->dim, xs, M, xmm, st);
+        for (int d = 0; d < p->dim; ++d) {
+            p->xlo[d] = xmm[2 * d];
+            p->xhi[d] = xmm[2 * d + 1];
+        }
+    }
+    double slo[3], shi[3];
+    for (int d = 0; d < p->dim; ++d) {
+        slo[d] = smm[2 * d];
+        shi[d] = smm[2 * d + 1];
+        if (!std::isfinite(slo[d]) || !std::isfinite(shi[d]) ||
+            !std::isfinite(p->xlo[d]) || !std::isfinite(p->xhi[d]))
+            fail(NUFFT_ERR_ARG, "non-finite type-3 coordinate");
+    }
+    size_t3(p, slo, shi);
+    // targets (gpu_t3.py:357-377)
+    CellParams cp{};
+    cp.kind = CELL_T3TGT;
+    cp.dim = p->dim;
+    const int prec = p->opts.prec;
+    cp.fp32 = !(prec == NUFFT_PREC_CRIT64 || prec == NUFFT_PREC_COORDS64);
+    cp.halfw = p->w2 / 2;
+    cp.halfw_d = p->w2 / 2.0;
+    for (int d = 0; d < p->dim; ++d) {
+        cp.n[d] = p->nup[d];
+        cp.a[d] = p->D[d];
+        cp.b[d] = p->hf[d] * p->gam[d];
+        cp.c[d] = 2.0 * kPi / (double)p->nup[d];
+        cp.e[d] = p->nup[d] / 2.0;
+        cp.m[d] = p->tg_tgt.m[d];
+        cp.nb[d] = p->tg_tgt.nb[d];
+    }
+    PhaseParams pp{};
+    pp.mode = 2;
+    pp.isign = p->isign;
+    pp.fp32 = !(prec == NUFFT_PREC_CRIT64 || prec == NUFFT_PREC_PHASES64);
+    for (int d = 0; d < p->dim; ++d) {
+        pp.C[d] = p->C[d];
+        pp.D[d] = p->D[d];
+    }
+    pp.ftd = p->d_ftd;
+    pp.fta = p->d_fta;
+    pp.nq = 128;
+    const bool tiled = want_tiled(p, N, p->tg_tgt);
+    const bool sort = tiled || p->opts.sort_points;
+    build_pointset(&p->tgt, cp, N, ss, sort, tiled, kMsubInterp, pp, p->d_err, st);
+    check_err_flag(p, st);
+    p->Ntgt = N;
+    // sources: guard against the extent only when it was given explicitly
+    set_sources_t3(p, M, xs, p->opts.has_source_extent != 0, st);
+    p->points_set = true;
+}
+
+// ---------------------------------------------------------------------
+void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
+                   int stage, cudaStream_t st) {
+    const size_t gbytes = sizeof(float2) * p->nupcells * nv;
+    if (p->type == 1) {
+        if (stage == NUFFT_STAGE_ALL || stage == NUFFT_STAGE_SPREAD) {
+            record(p, 0, st);
+            NUFFT_CUDA(cudaMemsetAsync(p->gfft, 0, gbytes, st));
+            launch_spread(p->src, p->tg_src, p->w, in, p->src.M, nv, p->gfft,
+                          p->nvg_src, st);
+            record(p, 1, st);
+        }
+        if (stage == NUFFT_STAGE_ALL || stage == NUFFT_STAGE_FINISH) {
+            if (stage == NUFFT_STAGE_FINISH) {
+                record(p, 0, st);
+                record(p, 1, st);
+            }
+            run_fft(p, p->gfft, nv, st);
+            record(p, 2, st);
+            launch_crop(p->dim, p->N, p->nup, p->dec, p->gfft, out, nv, st);
+            record(p, 3, st);
+        }
+    } else if (p->type == 2) {
+        record(p, 0, st);
+        launch_pad(p->dim, p->N, p->nup, p->dec, in, p->gfft, nv, st);
+        record(p, 1, st);
+        run_fft(p, p->gfft, nv, st);
+        record(p, 2, st);
+        launch_interp(p->src, p->tg_src, p->w, p->gfft, nv, out, p->src.M,
+                      p->nvg_src, st);
+        record(p, 3, st);
+    } else {
+        record(p, 0, st);
+        NUFFT_CUDA(cudaMemsetAsync(p->gspread, 0, sizeof(float2) * p->nfcells * nv, st));
+        launch_spread(p->src, p->tg_src, p->w, in, p->src.M, nv, p->gspread,
+                      p->nvg_src, st);
+        launch_pad(p->dim, p->nf, p->nup, p->dec, p->gspread, p->gfft, nv, st);
+        record(p, 1, st);
+        run_fft(p, p->gfft, nv, st);
+        record(p, 2, st);
+        launch_interp(p->tgt, p->tg_tgt, p->w2, p->gfft, nv, out, p->Ntgt,
+                      p->nvg_tgt, st);
+        record(p, 3, st);
+    }
+    p->ev_recorded = p->profile;
+}
+
+// Grow the number of fine grids held by the plan so that nvec vectors run
+// in one pass (shared point weights, one batched FFT), bounded by half of
+// the free device memory.  Only when opts.max_batch == 0 (automatic).
+void ensure_batch(nufft_plan_s* p, int nvec) {
+    if (nvec <= p->nbatch || p->opts.max_batch > 0) return;
+    size_t free_b = 0, tot = 0;
+    NUFFT_CUDA(cudaMemGetInfo(&free_b, &tot));
+    const size_t per = sizeof(float2) * (size_t)(p->nupcells + (p->type == 3 ? p->nfcells : 0));
+    const size_t have = per * (size_t)p->nbatch;
+    const int64_t cap = (int64_t)((free_b / 2 + have) / per);
+    const int nb = (int)std::min<int64_t>(nvec, std::max<int64_t>(cap, p->nbatch));
+    if (nb <= p->nbatch) return;
+    NUFFT_CUDA(cudaDeviceSynchronize());   // grids may still be in use
+    p->nbatch = nb;
+    alloc_grids(p);
+    p->nvg_src = vectors_per_tile(p->tg_src, p->nbatch);
+    if (p->type == 3) p->nvg_tgt = vectors_per_tile(p->tg_tgt, p->nbatch);
+}
+
+int64_t in_len(const nufft_plan_s* p) {
+    return p->type == 2 ? p->K : p->src.M;
+}
+int64_t out_len(const nufft_plan_s* p) {
+    return p->type == 1 ? p->K : (p->type == 2 ? p->src.M : p->Ntgt);
+}
+
+__global__ void k_split_cells(const int2* cell, int64_t n, int32_t* i1,
+                              float* fr) {
+    int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    int2 c = cell[j];
+    i1[j] = c.x;
+    fr[j] = __int_as_float(c.y);
+}
+
+__global__ void k_iota(uint32_t* p, int64_t n) {
+    int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (j < n) p[j] = (uint32_t)j;
+}
+
+// label window for execute_disjoint: out = groups - g0 if in [0, ng) else -1
+__global__ void k_window_labels(const int32_t* g, int64_t n, int g0, int ng,
+                                int32_t* out) {
+    int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    int v = g[j] - g0;
+    out[j] = (v >= 0 && v < ng) ? v : -1;
+}
+
+void window_labels(const int32_t* g, int64_t n, int g0, int ng,
+                         int32_t* out, cudaStream_t st) {
+    k_window_labels<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(g, n, g0, ng, out);
+    NUFFT_LAUNCH("k_window_labels");
+}
+
+}  // namespace nufft_impl
+
+using namespace nufft_impl;
+
+// =====================================================================
+// C ABI
+// =====================================================================
+extern "C" {
+
+void nufft_default_opts(nufft_opts* o) {
+    if (!o) return;
+    std::memset(o, 0, sizeof(*o));
+    o->prec = NUFFT_PREC_CRIT64;
+    o->method = NUFFT_METHOD_AUTO;
+    o->sort_points = 1;
+}
+
+int nufft_plan_create(int type, int dim, const int64_t* n_modes, int n_trans,
+                      double eps, int isign, const nufft_opts* opts, int device,
+                      nufft_plan_t* out) {
+    return guarded([&] {
+        if (!out) fail(NUFFT_ERR_ARG, "plan output pointer is NULL");
+        *out = nullptr;
+        if (type < 1 || type > 3) fail(NUFFT_ERR_ARG, "nufft_type must be 1, 2 or 3");
+        if (dim < 1 || dim > 3) fail(NUFFT_ERR_ARG, "dim must be 1, 2 or 3");
+        if (n_trans < 1) fail(NUFFT_ERR_ARG, "n_trans must be >= 1");
+        if (!(eps > 0.0)) fail(NUFFT_ERR_ARG, "eps must be positive");
+        if (type != 3 && !n_modes) fail(NUFFT_ERR_ARG, "n_modes is NULL");
+        int ndev = 0;
+        if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+            cudaGetLastError();
+            fail(NUFFT_ERR_CUDA, "no CUDA device available");
+        }
+        if (device < 0 || device >= ndev) fail(NUFFT_ERR_ARG, "invalid device ordinal");
+        DeviceGuard g(device);
+        nufft_plan_s* p = new nufft_plan_s();
+        try {
+            p->type = type;
+            p->dim = dim;
+            p->device = device;
+            p->n_trans = n_trans;
+            p->isign = isign >= 0 ? 1 : -1;
+            p->eps = eps;
+            if (opts) p->opts = *opts;
+            else nufft_default_opts(&p->opts);
+            if (p->opts.prec < 0 || p->opts.prec > 3) fail(NUFFT_ERR_ARG, "invalid prec");
+            if (type != 3 && (p->opts.prec == NUFFT_PREC_COORDS64 ||
+                              p->opts.prec == NUFFT_PREC_PHASES64))
+                fail(NUFFT_ERR_ARG, "prec must be 'fp32' or 'crit64' for types 1/2");
+            p->nbatch = p->opts.max_batch > 0 ? std::min(p->opts.max_batch, n_trans)
+                                              : n_trans;
+            p->profile = p->opts.profile != 0;
+            if (p->profile)
+                for (int i = 0; i < 4; ++i) NUFFT_CUDA(cudaEventCreate(&p->ev[i]));
+            p->d_err = (int*)dmalloc(sizeof(int), "error flag");
+            NUFFT_CUDA(cudaMemset(p->d_err, 0, sizeof(int)));
+            if (type != 3) {
+                for (int d = 0; d < dim; ++d) p->N[d] = n_modes[d];
+                create_t12(p);
+            } else {
+                create_t3(p);
+            }
+        } catch (...) {
+            nufft_plan_destroy(p);
+            throw;
+        }
+        *out = p;
+    });
+}
+
+int nufft_setpts(nufft_plan_t p, int64_t M, const double* x, const double* y,
+                 const double* z, int64_t N, const double* s, const double* t,
+                 const double* u, void* stream) {
+    return guarded([&] {
+        if (!p) fail(NUFFT_ERR_ARG, "NULL plan");
+        DeviceGuard g(p->device);
+        cudaStream_t st = (cudaStream_t)stream;
+        const double* xs[3] = {x, y, z};
+        for (int d = 0; d < p->dim; ++d)
+            if (!xs[d]) fail(NUFFT_ERR_ARG, "missing coordinate array");
+        if (p->type != 3) {
+            setpts_t12(p, M, xs, st);
+        } else {
+            const double* ss[3] = {s, t, u};
+            for (int d = 0; d < p->dim; ++d)
+                if (!ss[d]) fail(NUFFT_ERR_ARG, "missing target array");
+            setpts_t3(p, M, xs, N, ss, st);
+        }
+    });
+}
+
+int nufft_set_sources(nufft_plan_t p, int64_t M, const double* x,
+                      const double* y, const double* z, void* stream) {
+    return guarded([&] {
+        if (!p) fail(NUFFT_ERR_ARG, "NULL plan");
+        DeviceGuard g(p->device);
+        cudaStream_t st = (cudaStream_t)stream;
+        const double* xs[3] = {x, y, z};
+        for (int d = 0; d < p->dim; ++d)
+            if (!xs[d]) fail(NUFFT_ERR_ARG, "missing coordinate array");
+        if (p->type != 3) {
+            setpts_t12(p, M, xs, st);
+        } else {
+            if (!p->points_set) fail(NUFFT_ERR_STATE, "setpts() must be called first");
+            set_sources_t3(p, M, xs, true, st);
+        }
+    });
+}
+
+int nufft_execute_stage(nufft_plan_t p, int stage, const void* in, void* out,
+                        int nvec, void* stream) {
+    return guarded([&] {
+        if (!p) fail(NUFFT_ERR_ARG, "NULL plan");
+        if (!p->points_set) fail(NUFFT_ERR_STATE, "setpts() must be called before execute()");
+        if (nvec < 1) fail(NUFFT_ERR_ARG, "nvec must be >= 1");
+        if (stage != NUFFT_STAGE_ALL) {
+            if (p->type != 1) fail(NUFFT_ERR_ARG, "stages apply to type-1 plans only");
+            if (nvec > p->nbatch) fail(NUFFT_ERR_ARG, "staged execute: nvec exceeds the plan batch");
+            if (stage != NUFFT_STAGE_SPREAD && stage != NUFFT_STAGE_FINISH)
+                fail(NUFFT_ERR_ARG, "unknown stage");
+        }
+        if ((stage == NUFFT_STAGE_ALL || stage == NUFFT_STAGE_SPREAD) && !in)
+            fail(NUFFT_ERR_ARG, "NULL input pointer");
+        if ((stage == NUFFT_STAGE_ALL || stage == NUFFT_STAGE_FINISH) && !out)
+            fail(NUFFT_ERR_ARG, "NULL output pointer");
+        DeviceGuard g(p->device);
+        cudaStream_t st = (cudaStream_t)stream;
+        if (stage == NUFFT_STAGE_ALL) ensure_batch(p, nvec);
+        const float2* fin = (const float2*)in;
+        float2* fout = (float2*)out;
+        const int64_t il = in_len(p), ol = out_len(p);
+        for (int v0 = 0; v0 < nvec; v0 += p->nbatch) {
+            const int nv = std::min(p->nbatch, nvec - v0);
+            execute_chunk(p, fin ? fin + v0 * il : nullptr,
+                          fout ? fout + v0 * ol : nullptr, nv, stage, st);
+        }
+    });
+}
+
+int nufft_execute(nufft_plan_t p, const void* in, void* out, int nvec,
+                  void* stream) {
+    if (!in || !out) {
+        set_last_error("NULL data pointer");
+        return NUFFT_ERR_ARG;
+    }
+    return nufft_execute_stage(p, NUFFT_STAGE_ALL, in, out, nvec, stream);
+}
+
+int nufft_get_grid(nufft_plan_t p, void** grid, int64_t* n_complex) {
+    return guarded([&] {
+        if (!p) fail(NUFFT_ERR_ARG, "NULL plan");
+        if (grid) *grid = p->gfft;
+        if (n_complex) *n_complex = p->nupcells * p->nbatch;
+    });
+}
+
+int nufft_execute_disjoint(nufft_plan_t p, const void* c, const int32_t* groups,
+                           int ngroups, void* out, void* stream) {
+    return guarded([&] {
+        if (!p) fail(NUFFT_ERR_ARG, "NULL plan");
+        if (p->type != 1) fail(NUFFT_ERR_ARG, "execute_disjoint applies to type-1 plans");
+        if (!p->points_set) fail(NUFFT_ERR_STATE, "setpts() must be called before execute()");
+        if (ngroups < 0) fail(NUFFT_ERR_ARG, "ngroups must be >= 0");
+        DeviceGuard g(p->device);
+        cudaStream_t st = (cudaStream_t)stream;
+        const float2* fc = (const float2*)c;
+        float2* fo = (float2*)out;
+        // groups processed nbatch at a time; a group index outside the
+        // current window is skipped by offsetting the labels on the fly.
+        int32_t* shifted = (int32_t*)dmalloc(sizeof(int32_t) * p->src.M, "group labels");
+        try {
+            for (int g0 = 0; g0 < ngroups; g0 += p->nbatch) {
+                const int ng = std::min(p->nbatch, ngroups - g0);
+                NUFFT_CUDA(cudaMemsetAsync(p->gfft, 0, sizeof(float2) * p->nupcells * ng, st));
+                // labels relative to this window; out-of-window -> -1
+                window_labels(groups, p->src.M, g0, ng, shifted, st);
+                launch_spread_groups(p->src, p->tg_src, p->w, fc, shifted, p->gfft, st);
+                run_fft(p, p->gfft, ng, st);
+                launch_crop(p->dim, p->N, p->nup, p->dec, p->gfft, fo + (int64_t)g0 * p->K,
+                            ng, st);
+            }
+        } catch (...) {
+            NUFFT_CUDA(cudaStreamSynchronize(st));
+            dfree(shifted);
+            throw;
+        }
+        NUFFT_CUDA(cudaStreamSynchronize(st));
+        dfree(shifted);
+    });
+}
+
+int nufft_plan_destroy(nufft_plan_t p) {
+    if (!p) return NUFFT_OK;
+    return guarded([&] {
+        int cur = 0;
+        cudaGetDevice(&cur);
+        cudaSetDevice(p->device);
+        cudaDeviceSynchronize();
+        destroy_ffts(p);
+        free_pointset(&p->src);
+        free_pointset(&p->tgt);
+        for (int d = 0; d < 3; ++d) dfree(p->dec[d]);
+        dfree(p->gfft);
+        dfree(p->gspread);
+        dfree(p->d_ftd);
+        dfree(p->d_fta);
+        dfree(p->d_err);
+        for (int i = 0; i < 4; ++i)
+            if (p->ev[i]) cudaEventDestroy(p->ev[i]);
+        cudaSetDevice(cur);
+        delete p;
+    });
+}
+
+int nufft_plan_get_info(nufft_plan_t p, nufft_plan_info* info) {
+    return guarded([&] {
+        if (!p || !info) fail(NUFFT_ERR_ARG, "NULL argument");
+        std::memset(info, 0, sizeof(*info));
+        info->type = p->type;
+        info->dim = p->dim;
+        info->n_trans = p->n_trans;
+        info->isign = p->isign;
+        info->w = p->w;
+        info->w2 = p->w2;
+        info->beta = p->beta;
+        info->beta2 = p->beta2;
+        info->eps = p->eps;
+        info->upsampfac = p->sigma;
+        info->sigma_inner = p->sigma_in;
+        for (int d = 0; d < 3; ++d) {
+            info->n_modes[d] = p->N[d];
+            info->nf[d] = p->nf[d];
+            info->n_up[d] = p->nup[d];
+            info->C[d] = p->C[d];
+            info->D[d] = p->D[d];
+            info->gam[d] = p->gam[d];
+            info->bin[d] = p->tg_src.m[d];
+        }
+        info->M = p->src.M;
+        info->N_tgt = p->Ntgt;
+        info->tiled = p->src.tiled ? 1 : 0;
+        info->nsub = p->src.nsub;
+        info->nsub_tgt = p->tgt.nsub;
+        int64_t b = sizeof(float2) * (p->nupcells * p->nbatch);
+        if (p->type == 3) b += sizeof(float2) * p->nfcells * p->nbatch;
+        b += p->src.cap * (8 * p->dim + 4 + (p->src.phase ? 8 : 0));
+        b += p->tgt.cap * (8 * p->dim + 4 + (p->tgt.phase ? 8 : 0));
+        info->device_bytes = b;
+    });
+}
+
+int nufft_get_stage_times(nufft_plan_t p, float* ms, int n) {
+    int count = 0;
+    int rc = guarded([&] {
+        if (!p) fail(NUFFT_ERR_ARG, "NULL plan");
+        if (!p->profile) fail(NUFFT_ERR_STATE, "plan was not created with opts.profile = 1");
+        if (!p->ev_recorded) fail(NUFFT_ERR_STATE, "no execute has been recorded");
+        NUFFT_CUDA(cudaEventSynchronize(p->ev[3]));
+        float t[4];
+        for (int i = 0; i < 3; ++i)
+            NUFFT_CUDA(cudaEventElapsedTime(&t[i], p->ev[i], p->ev[i + 1]));
+        NUFFT_CUDA(cudaEventElapsedTime(&t[3], p->ev[0], p->ev[3]));
+        for (int i = 0; i < 4 && i < n; ++i) ms[i] = t[i];
+        count = 4;
+    });
+    return rc == NUFFT_OK ? count : rc;
+}
+
+int nufft_plan_set_profile(nufft_plan_t p, int on) {
+    return guarded([&] {
+        if (!p) fail(NUFFT_ERR_ARG, "NULL plan");
+        DeviceGuard g(p->device);
+        if (on && !p->ev[0])
+            for (int i = 0; i < 4; ++i) NUFFT_CUDA(cudaEventCreate(&p->ev[i]));
+        p->profile = on != 0;
+        if (!p->profile) p->ev_recorded = false;
+    });
+}
+
+int nufft_debug_points(nufft_plan_t p, int which, int32_t* i1, float* fr,
+                       uint32_t* perm, void* stream) {
+    return guarded([&] {
+        if (!p) fail(NUFFT_ERR_ARG, "NULL plan");
+        if (!p->points_set) fail(NUFFT_ERR_STATE, "setpts() has not been called");
+        const PointSet& ps = which == 0 ? p->src : p->tgt;
+        if (which == 1 && p->type != 3) fail(NUFFT_ERR_ARG, "targets exist for type 3 only");
+        DeviceGuard g(p->device);
+        cudaStream_t st = (cudaStream_t)stream;
+        const unsigned blocks = (unsigned)((ps.M + 255) / 256);
+        for (int d = 0; d < p->dim; ++d) {
+            if (i1 && fr) {
+                k_split_cells<<<blocks, 256, 0, st>>>(ps.cell[d], ps.M, i1 + d * ps.M,
+                                                      fr + d * ps.M);
+                NUFFT_LAUNCH("k_split_cells");
+            }
+        }
+        if (perm) {
+            if (ps.sorted)
+                NUFFT_CUDA(cudaMemcpyAsync(perm, ps.perm, 4 * ps.M,
+                                           cudaMemcpyDeviceToDevice, st));
+            else {
+                k_iota<<<blocks, 256, 0, st>>>(perm, ps.M);
+                NUFFT_LAUNCH("k_iota");
+            }
+        }
+    });
+}
+
+int nufft_expi(int ncomp, const double* const* comps, int64_t n, int isign,
+               void* out, void* stream) {
+    return guarded([&] {
+        if (!comps || (!out && n > 0)) fail(NUFFT_ERR_ARG, "NULL argument");
+        for (int c = 0; c < ncomp; ++c)
+            if (!comps[c] && n > 0) fail(NUFFT_ERR_ARG, "NULL phase component");
+        launch_expi(ncomp, comps, n, isign, (float2*)out, (cudaStream_t)stream);
+    });
+}
+
+int nufft_kernel_params(double eps, double upsampfac, int* w, double* beta) {
+    return guarded([&] {
+        if (!w || !beta) fail(NUFFT_ERR_ARG, "NULL output");
+        if (!(eps > 0.0)) fail(NUFFT_ERR_ARG, "eps must be positive");
+        kernel_params(eps, upsampfac, w, beta);
+    });
+}
+
+int64_t nufft_next235even(int64_t n) { return next235even(n); }
+
+int nufft_kernel_ft(int64_t n, const double* xi, double beta, int w, double* out) {
+    return guarded([&] {
+        if (n > 0 && (!xi || !out)) fail(NUFFT_ERR_ARG, "NULL argument");
+        std::vector<double> dq, aq;
+        kernel_ft_nodes(beta, w, &dq, &aq);
+        for (int64_t i = 0; i < n; ++i) out[i] = phihat_host(xi[i], dq, aq);
+    });
+}
+
+int nufft_set_nhg_type3(double S, double X, double upsampfac, int w,
+                        int64_t* nf, double* h, double* gam) {
+    return guarded([&] {
+        if (!nf || !h || !gam) fail(NUFFT_ERR_ARG, "NULL output");
+        set_nhg_type3(S, X, upsampfac, w, nf, h, gam);
+    });
+}
+
+int nufft_last_error(char* buf, int len) {
+    const std::string& e = nufft::g_last_error;
+    if (buf && len > 0) {
+        const int n = std::min<int>(len - 1, (int)e.size());
+        std::memcpy(buf, e.data(), n);
+        buf[n] = 0;
+    }
+    return (int)e.size();
+}
+
+const char* nufft_version(void) { return "nufft_b200 0.1.0 (sm_100a)"; }
+
+int nufft_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+}  // extern "C"
+

@@ -1,0 +1,426 @@
+// points.cu -- device setpts: coordinate rescale to (cell, fraction),
+// counting-sort by bin, subproblem tables, and the type-3 pre/post phases.
+//
+// The reference does this on the host in numpy fp64 ("crit64",
+// mlx_nufft/nd.py:152-181, 298-372; mlx_nufft/gpu_t3.py:344-377, 474-501)
+// or with a double-single Metal kernel plus mx.argsort (nd.py:43-91,
+// 191-243; gpu_t3.py:237-276, 508-555).  B200 has native fp64, so every
+// rescale below is the reference's fp64 expression evaluated with the same
+// operations in the same order (IEEE-exact fmod, correctly rounded + - * /,
+// ceil), which makes the cell index bit-identical to the host fp64 path.
+// The sort is a counting sort: one atomic histogram pass that also records
+// each point's rank inside its bin, an exclusive scan of the bin counts,
+// and a scatter -- O(M) with two coalesced reads of the coordinates.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+
+#include "internal.h"
+
+namespace nufft {
+
+struct Coords {
+    const double* p[3];
+};
+
+// (i1, fr) of coordinate x in dimension d, plus the bin-normalised cell
+// index: i1 is shifted by a multiple of the grid size so that
+// i1 + w/2 lies in [0, n) (the grid is periodic, so this changes no tap).
+__device__ __forceinline__ void cell_of(const CellParams& cp, int d, double x,
+                                        int* i1n, float* fr, int* ib,
+                                        bool* bad) {
+    if (!isfinite(x)) {
+        *bad = true;
+        x = 0.0;
+    }
+    int i1;
+    if (cp.kind == CELL_FOLD) {
+        // xi = mod(x, 2pi) / h ; numpy's float mod: fmod, then + 2pi when
+        // the remainder is negative (nd.py:162)
+        double r = fmod(x, kTwoPi);
+        if (r < 0.0) r += kTwoPi;
+        if (!cp.fp32) {
+            double xi = r / cp.h[d];
+            double i1d = ceil(xi - cp.halfw_d);
+            i1 = (int)i1d;
+            *fr = (float)(xi - i1d);
+        } else {
+            float xi = (float)r / (float)cp.h[d];
+            float i1f = ceilf(xi - (float)cp.halfw_d);
+            i1 = (int)i1f;
+            *fr = xi - i1f;
+        }
+    } else if (cp.kind == CELL_T3SRC) {
+        // xi = (x - C) / gam / h + nf/2  (gpu_t3.py:486-490)
+        if (!cp.fp32) {
+            double xi = (x - cp.a[d]) / cp.b[d] / cp.h[d] + cp.c[d];
+            double i1d = ceil(xi - cp.halfw_d);
+            i1 = (int)i1d;
+            *fr = (float)(xi - i1d);
+        } else {
+            float xi = ((float)x - (float)cp.a[d]) / (float)cp.b[d] /
+                           (float)cp.h[d] + (float)cp.c[d];
+            float i1f = ceilf(xi - (float)cp.halfw_d);
+            i1 = (int)i1f;
+            *fr = xi - i1f;
+        }
+    } else {
+        // theta = (s - D) * (h*gam); lam = theta / (2pi/n_up) + n_up/2
+        // (gpu_t3.py:357-366)
+        if (!cp.fp32) {
+            double th = (x - cp.a[d]) * cp.b[d];
+            double lam = th / cp.c[d] + cp.e[d];
+            double i1d = ceil(lam - cp.halfw_d);
+            i1 = (int)i1d;
+            *fr = (float)(lam - i1d);
+        } else {
+            float th = ((float)x - (float)cp.a[d]) * (float)cp.b[d];
+            float lam = th / (float)cp.c[d] + (float)cp.e[d];
+            float i1f = ceilf(lam - (float)cp.halfw_d);
+            i1 = (int)i1f;
+            *fr = lam - i1f;
+        }
+    }
+    // periodic normalisation for binning
+    int64_t n = cp.n[d];
+    int64_t b = ((int64_t)i1 + cp.halfw) % n;
+    if (b < 0) b += n;
+    *ib = (int)b;
+    *i1n = (int)(b - cp.halfw);
+}
+
+template <int DIM>
+__global__ void k_cells_direct(int64_t M, Coords X, CellParams cp, int2* c0,
+                               int2* c1, int2* c2, int* err) {
+    int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (j >= M) return;
+    bool bad = false;
+    int2* out[3] = {c0, c1, c2};
+#pragma unroll
+    for (int d = 0; d < DIM; ++d) {
+        int i1, ib;
+        float fr;
+        cell_of(cp, d, X.p[d][j], &i1, &fr, &ib, &bad);
+        out[d][j] = make_int2(i1, __float_as_int(fr));
+    }
+    if (bad) atomicOr(err, 1);
+}
+
+template <int DIM>
+__global__ void k_bin_count(int64_t M, Coords X, CellParams cp,
+                            uint32_t* key_of, uint32_t* rank_of,
+                            uint32_t* count, int* err) {
+    int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (j >= M) return;
+    bool bad = false;
+    uint32_t key = 0;
+#pragma unroll
+    for (int d = 0; d < DIM; ++d) {
+        int i1, ib;
+        float fr;
+        cell_of(cp, d, X.p[d][j], &i1, &fr, &ib, &bad);
+        key = key * (uint32_t)cp.nb[d] + (uint32_t)(ib / cp.m[d]);
+    }
+    if (bad) atomicOr(err, 1);
+    key_of[j] = key;
+    rank_of[j] = atomicAdd(&count[key], 1u);
+}
+
+template <int DIM>
+__global__ void k_bin_scatter(int64_t M, Coords X, CellParams cp,
+                              const uint32_t* key_of, const uint32_t* rank_of,
+                              const uint32_t* start, int2* c0, int2* c1,
+                              int2* c2, uint32_t* perm) {
+    int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (j >= M) return;
+    bool bad = false;
+    uint32_t pos = start[key_of[j]] + rank_of[j];
+    int2* out[3] = {c0, c1, c2};
+#pragma unroll
+    for (int d = 0; d < DIM; ++d) {
+        int i1, ib;
+        float fr;
+        cell_of(cp, d, X.p[d][j], &i1, &fr, &ib, &bad);
+        out[d][pos] = make_int2(i1, __float_as_int(fr));
+    }
+    perm[pos] = (uint32_t)j;
+}
+
+// Single-CTA exclusive scan (uint32, in place allowed) with the total in
+// *total.  Only used at setpts time on bin / subproblem counts.
+__global__ void __launch_bounds__(1024)
+k_scan(const uint32_t* in, uint32_t* out, int64_t n, uint32_t* total) {
+    __shared__ uint32_t sums[1024];
+    const int t = threadIdx.x;
+    const int64_t chunk = (n + 1023) / 1024;
+    const int64_t b = t * chunk;
+    const int64_t e = min(n, b + chunk);
+    uint32_t s = 0;
+    for (int64_t i = b; i < e; ++i) s += in[i];
+    sums[t] = s;
+    __syncthreads();
+    for (int off = 1; off < 1024; off <<= 1) {
+        uint32_t v = (t >= off) ? sums[t - off] : 0u;
+        __syncthreads();
+        sums[t] += v;
+        __syncthreads();
+    }
+    uint32_t run = t ? sums[t - 1] : 0u;
+    for (int64_t i = b; i < e; ++i) {
+        uint32_t v = in[i];
+        out[i] = run;
+        run += v;
+    }
+    if (t == 1023) *total = sums[1023];
+}
+
+__global__ void k_sub_count(const uint32_t* count, int64_t nbins, int msub,
+                            uint32_t* nsubs) {
+    int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (b >= nbins) return;
+    nsubs[b] = (count[b] + (uint32_t)msub - 1u) / (uint32_t)msub;
+}
+
+__global__ void k_sub_fill(const uint32_t* count, const uint32_t* start,
+                           const uint32_t* subofs, int64_t nbins, int msub,
+                           int4* subs) {
+    int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (b >= nbins) return;
+    uint32_t n = count[b];
+    uint32_t k0 = subofs[b];
+    for (uint32_t k = 0; k * (uint32_t)msub < n; ++k) {
+        uint32_t s = start[b] + k * (uint32_t)msub;
+        uint32_t c = min((uint32_t)msub, n - k * (uint32_t)msub);
+        subs[k0 + k] = make_int4((int)s, (int)c, (int)b, 0);
+    }
+}
+
+// Type-3 phases, written in sorted order (position j reads caller index
+// perm[j]).
+//  mode 1: prephase e^{i isign sum_d D_d x_d}            (gpu_t3.py:491-493)
+//  mode 2: post e^{i isign sum_d C_d (s_d - D_d)} / prod_d phihat(theta_d)
+//          with theta_d = (s_d - D_d) * (h_d gam_d)       (gpu_t3.py:368-377)
+template <int DIM>
+__global__ void k_phase(int64_t M, Coords X, const uint32_t* perm,
+                        PhaseParams pp, CellParams cp, float2* phase) {
+    int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (j >= M) return;
+    int64_t src = perm ? (int64_t)perm[j] : j;
+    double ang;
+    if (!pp.fp32) {
+        ang = 0.0;
+#pragma unroll
+        for (int d = 0; d < DIM; ++d) {
+            double v = X.p[d][src];
+            ang += (pp.mode == 1) ? pp.D[d] * v : pp.C[d] * (v - pp.D[d]);
+        }
+    } else {
+        float a = 0.0f;
+#pragma unroll
+        for (int d = 0; d < DIM; ++d) {
+            float v = (float)X.p[d][src];
+            a += (pp.mode == 1) ? (float)pp.D[d] * v
+                                : (float)pp.C[d] * (v - (float)pp.D[d]);
+        }
+        ang = (double)a;
+    }
+    double sn, cs;
+    sincos((double)pp.isign * ang, &sn, &cs);
+    if (pp.mode == 2) {
+        double tdec = 1.0;
+#pragma unroll
+        for (int d = 0; d < DIM; ++d) {
+            double s = X.p[d][src];
+            double th;
+            if (!cp.fp32)
+                th = (s - cp.a[d]) * cp.b[d];
+            else
+                th = (double)(((float)s - (float)cp.a[d]) * (float)cp.b[d]);
+            double acc = 0.0;
+            for (int q = 0; q < pp.nq; ++q) acc += pp.fta[q] * cos(th * pp.ftd[q]);
+            tdec *= 2.0 * acc;
+        }
+        cs /= tdec;
+        sn /= tdec;
+    }
+    phase[j] = make_float2((float)cs, (float)sn);
+}
+
+// Partial min/max of up to 6 arrays: partial[blk][2*i] = min, [2*i+1] = max.
+struct Arr6 {
+    const double* p[6];
+};
+__global__ void k_minmax(int n, Arr6 A, int64_t M, double* partial) {
+    __shared__ double smin[6][256], smax[6][256];
+    const int t = threadIdx.x;
+    for (int i = 0; i < n; ++i) {
+        double lo = INFINITY, hi = -INFINITY;
+        for (int64_t j = blockIdx.x * (int64_t)blockDim.x + t; j < M;
+             j += (int64_t)gridDim.x * blockDim.x) {
+            double v = A.p[i][j];
+            lo = fmin(lo, v);
+            hi = fmax(hi, v);
+        }
+        smin[i][t] = lo;
+        smax[i][t] = hi;
+    }
+    __syncthreads();
+    for (int s = 128; s > 0; s >>= 1) {
+        if (t < s)
+            for (int i = 0; i < n; ++i) {
+                smin[i][t] = fmin(smin[i][t], smin[i][t + s]);
+                smax[i][t] = fmax(smax[i][t], smax[i][t + s]);
+            }
+        __syncthreads();
+    }
+    if (t == 0)
+        for (int i = 0; i < n; ++i) {
+            partial[blockIdx.x * 2 * n + 2 * i] = smin[i][0];
+            partial[blockIdx.x * 2 * n + 2 * i + 1] = smax[i][0];
+        }
+}
+
+void device_minmax(int n, const double* const* arrs, int64_t M, double* out,
+                   cudaStream_t st) {
+    Arr6 A{};
+    for (int i = 0; i < n; ++i) A.p[i] = arrs[i];
+    int blocks = (int)std::min<int64_t>(512, (M + 255) / 256);
+    if (blocks < 1) blocks = 1;
+    double* d_part = (double*)dmalloc(sizeof(double) * blocks * 2 * n, "minmax");
+    k_minmax<<<blocks, 256, 0, st>>>(n, A, M, d_part);
+    NUFFT_LAUNCH("k_minmax");
+    std::vector<double> h(blocks * 2 * n);
+    NUFFT_CUDA(cudaMemcpyAsync(h.data(), d_part, sizeof(double) * h.size(),
+                               cudaMemcpyDeviceToHost, st));
+    NUFFT_CUDA(cudaStreamSynchronize(st));
+    dfree(d_part);
+    for (int i = 0; i < n; ++i) {
+        double lo = INFINITY, hi = -INFINITY;
+        for (int b = 0; b < blocks; ++b) {
+            lo = std::min(lo, h[b * 2 * n + 2 * i]);
+            hi = std::max(hi, h[b * 2 * n + 2 * i + 1]);
+        }
+        out[2 * i] = lo;
+        out[2 * i + 1] = hi;
+    }
+}
+
+void free_pointset(PointSet* ps) {
+    for (int d = 0; d < 3; ++d) {
+        dfree(ps->cell[d]);
+        ps->cell[d] = nullptr;
+    }
+    dfree(ps->perm);
+    dfree(ps->subs);
+    dfree(ps->phase);
+    ps->perm = nullptr;
+    ps->subs = nullptr;
+    ps->phase = nullptr;
+    ps->cap = ps->subcap = ps->M = ps->nsub = 0;
+}
+
+namespace {
+
+template <int DIM>
+void build_impl(PointSet* ps, const CellParams& cp, int64_t M,
+                const double* const* coords, bool sort, bool tiled, int msub,
+                const PhaseParams& pp, int* d_err, cudaStream_t st) {
+    Coords X{};
+    for (int d = 0; d < DIM; ++d) X.p[d] = coords[d];
+    const int bs = 256;
+    const int64_t grid = (M + bs - 1) / bs;
+    if (!sort) {
+        k_cells_direct<DIM><<<(unsigned)grid, bs, 0, st>>>(
+            M, X, cp, ps->cell[0], ps->cell[1], ps->cell[2], d_err);
+        NUFFT_LAUNCH("k_cells_direct");
+    } else {
+        int64_t nbins = 1;
+        for (int d = 0; d < DIM; ++d) nbins *= cp.nb[d];
+        if (nbins > (int64_t)0xffffffffLL) fail(-1, "too many bins");
+        uint32_t* key_of = (uint32_t*)dmalloc(4 * M, "sort keys");
+        uint32_t* rank_of = (uint32_t*)dmalloc(4 * M, "sort ranks");
+        uint32_t* count = (uint32_t*)dmalloc(4 * (nbins + 1), "bin counts");
+        uint32_t* start = (uint32_t*)dmalloc(4 * (nbins + 1), "bin starts");
+        uint32_t* tot = (uint32_t*)dmalloc(8, "scan total");
+        NUFFT_CUDA(cudaMemsetAsync(count, 0, 4 * (nbins + 1), st));
+        k_bin_count<DIM><<<(unsigned)grid, bs, 0, st>>>(M, X, cp, key_of,
+                                                       rank_of, count, d_err);
+        NUFFT_LAUNCH("k_bin_count");
+        k_scan<<<1, 1024, 0, st>>>(count, start, nbins, tot);
+        NUFFT_LAUNCH("k_scan");
+        k_bin_scatter<DIM><<<(unsigned)grid, bs, 0, st>>>(
+            M, X, cp, key_of, rank_of, start, ps->cell[0], ps->cell[1],
+            ps->cell[2], ps->perm);
+        NUFFT_LAUNCH("k_bin_scatter");
+        ps->nsub = 0;
+        if (tiled) {
+            uint32_t* nsubs = (uint32_t*)dmalloc(4 * (nbins + 1), "nsubs");
+            uint32_t* subofs = (uint32_t*)dmalloc(4 * (nbins + 1), "subofs");
+            const unsigned gb = (unsigned)((nbins + 255) / 256);
+            k_sub_count<<<gb, 256, 0, st>>>(count, nbins, msub, nsubs);
+            NUFFT_LAUNCH("k_sub_count");
+            k_scan<<<1, 1024, 0, st>>>(nsubs, subofs, nbins, tot);
+            NUFFT_LAUNCH("k_scan");
+            uint32_t h_tot = 0;
+            NUFFT_CUDA(cudaMemcpyAsync(&h_tot, tot, 4, cudaMemcpyDeviceToHost, st));
+            NUFFT_CUDA(cudaStreamSynchronize(st));
+            if ((int64_t)h_tot > ps->subcap) {
+                dfree(ps->subs);
+                ps->subs = nullptr;
+                ps->subcap = 0;
+                ps->subs = (int4*)dmalloc(sizeof(int4) * std::max<int64_t>(h_tot, 1),
+                                          "subproblems");
+                ps->subcap = std::max<int64_t>(h_tot, 1);
+            }
+            k_sub_fill<<<gb, 256, 0, st>>>(count, start, subofs, nbins, msub,
+                                           ps->subs);
+            NUFFT_LAUNCH("k_sub_fill");
+            ps->nsub = h_tot;
+            NUFFT_CUDA(cudaStreamSynchronize(st));
+            dfree(nsubs);
+            dfree(subofs);
+        }
+        NUFFT_CUDA(cudaStreamSynchronize(st));
+        dfree(key_of);
+        dfree(rank_of);
+        dfree(count);
+        dfree(start);
+        dfree(tot);
+    }
+    if (pp.mode) {
+        k_phase<DIM><<<(unsigned)grid, bs, 0, st>>>(
+            M, X, sort ? ps->perm : nullptr, pp, cp, ps->phase);
+        NUFFT_LAUNCH("k_phase");
+    }
+}
+
+}  // namespace
+
+void build_pointset(PointSet* ps, const CellParams& cp, int64_t M,
+                    const double* const* coords, bool sort, bool tiled,
+                    int msub, const PhaseParams& pp, int* d_err,
+                    cudaStream_t st) {
+    if (M < 1) fail(-1, "at least one nonuniform point is required");
+    if (M >= (int64_t)0x7fffffffLL)
+        fail(-1, "at most 2^31-1 nonuniform points per plan");
+    if (M > ps->cap || (sort && !ps->perm) || (pp.mode && !ps->phase)) {
+        free_pointset(ps);
+        for (int d = 0; d < cp.dim; ++d)
+            ps->cell[d] = (int2*)dmalloc(sizeof(int2) * M, "point cells");
+        ps->perm = (uint32_t*)dmalloc(4 * M, "point permutation");
+        if (pp.mode) ps->phase = (float2*)dmalloc(sizeof(float2) * M, "phases");
+        ps->cap = M;
+    }
+    ps->dim = cp.dim;
+    ps->M = M;
+    ps->sorted = sort;
+    ps->tiled = tiled && sort;
+    switch (cp.dim) {
+        case 1: build_impl<1>(ps, cp, M, coords, sort, tiled, msub, pp, d_err, st); break;
+        case 2: build_impl<2>(ps, cp, M, coords, sort, tiled, msub, pp, d_err, st); break;
+        case 3: build_impl<3>(ps, cp, M, coords, sort, tiled, msub, pp, d_err, st); break;
+        default: fail(-1, "dim must be 1, 2 or 3");
+    }
+}
+
+}  // namespace nufft

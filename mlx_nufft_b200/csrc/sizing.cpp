@@ -1,0 +1,146 @@
+// sizing.cpp -- host fp64 numerics of the NUFFT plan: kernel width/shape,
+// fine-grid sizes and the kernel Fourier transform.  Each function restates
+// the algorithm of the reference's mlx_nufft/sizing.py (itself FINUFFT's
+// setup_spreader / set_nhg_type3) so that grid sizes and kernel shapes agree
+// exactly with the reference.
+#include <algorithm>
+#include <cmath>
+#include <vector>
+
+#include "internal.h"
+
+namespace nufft {
+
+// Smallest even n' >= n whose prime factors are all in {2, 3, 5}.
+// mlx_nufft/sizing.py:13-25
+int64_t next235even(int64_t n) {
+    if (n < 2) n = 2;
+    if (n % 2) n += 1;
+    for (;; n += 2) {
+        int64_t m = n;
+        while (m % 2 == 0) m /= 2;
+        while (m % 3 == 0) m /= 3;
+        while (m % 5 == 0) m /= 5;
+        if (m == 1) return n;
+    }
+}
+
+// ES width w and shape beta for tolerance eps at upsampling sigma.
+// mlx_nufft/sizing.py:28-50
+void kernel_params(double eps, double upsampfac, int* w, double* beta) {
+    int ns;
+    if (upsampfac == 2.0)
+        ns = (int)std::ceil(-std::log10(eps / 10.0));
+    else
+        ns = (int)std::ceil(-std::log(eps) /
+                            (kPi * std::sqrt(1.0 - 1.0 / upsampfac)));
+    if (ns < 2) ns = 2;
+    if (ns > 16) ns = 16;
+    double betaoverns = 2.30;
+    if (ns == 2) betaoverns = 2.20;
+    else if (ns == 3) betaoverns = 2.26;
+    else if (ns == 4) betaoverns = 2.38;
+    if (upsampfac != 2.0)
+        betaoverns = 0.97 * kPi * (1.0 - 1.0 / (2.0 * upsampfac));
+    *w = ns;
+    *beta = betaoverns * ns;
+}
+
+namespace {
+
+// Gauss-Legendre nodes/weights on [-1, 1] (ascending nodes), by Newton's
+// method on the three-term Legendre recurrence.
+void gauss_legendre(int n, std::vector<double>* x, std::vector<double>* wt) {
+    x->assign(n, 0.0);
+    wt->assign(n, 0.0);
+    for (int i = 0; i < (n + 1) / 2; ++i) {
+        double z = std::cos(kPi * (i + 0.75) / (n + 0.5));
+        double dp = 0.0;
+        for (int it = 0; it < 100; ++it) {
+            double p0 = 1.0, p1 = z;
+            for (int k = 2; k <= n; ++k) {
+                double p2 = ((2.0 * k - 1.0) * z * p1 - (k - 1.0) * p0) / k;
+                p0 = p1;
+                p1 = p2;
+            }
+            dp = n * (z * p1 - p0) / (z * z - 1.0);
+            double dz = p1 / dp;
+            z -= dz;
+            if (std::fabs(dz) < 1e-16) break;
+        }
+        {   // weight from the converged node
+            double p0 = 1.0, p1 = z;
+            for (int k = 2; k <= n; ++k) {
+                double p2 = ((2.0 * k - 1.0) * z * p1 - (k - 1.0) * p0) / k;
+                p0 = p1;
+                p1 = p2;
+            }
+            dp = n * (z * p1 - p0) / (z * z - 1.0);
+        }
+        double wi = 2.0 / ((1.0 - z * z) * dp * dp);
+        (*x)[n - 1 - i] = z;
+        (*x)[i] = -z;
+        (*wt)[i] = wi;
+        (*wt)[n - 1 - i] = wi;
+    }
+}
+
+double es_kernel64(double d, double beta, int w) {
+    double z = 2.0 * d / w;
+    double z2 = z * z;
+    if (z2 > 1.0) return 0.0;
+    return std::exp(beta * (std::sqrt(1.0 - z2) - 1.0));
+}
+
+}  // namespace
+
+// Nodes d_q in [0, w/2] and weights a_q (quadrature weight times kernel
+// value) so that phihat(xi) = 2 * sum_q a_q cos(xi * d_q).
+// mlx_nufft/sizing.py:74-85 (nquad = 128)
+void kernel_ft_nodes(double beta, int w, std::vector<double>* d,
+                     std::vector<double>* a) {
+    const int nq = 128;
+    std::vector<double> x, wt;
+    gauss_legendre(nq, &x, &wt);
+    d->resize(nq);
+    a->resize(nq);
+    for (int q = 0; q < nq; ++q) {
+        (*d)[q] = 0.5 * (x[q] + 1.0) * (w / 2.0);
+        (*a)[q] = wt[q] * (w / 4.0) * es_kernel64((*d)[q], beta, w);
+    }
+}
+
+double kernel_ft(double xi, double beta, int w) {
+    std::vector<double> d, a;
+    kernel_ft_nodes(beta, w, &d, &a);
+    double s = 0.0;
+    for (size_t q = 0; q < d.size(); ++q) s += a[q] * std::cos(xi * d[q]);
+    return 2.0 * s;
+}
+
+// Type-3 spread-grid size nf, spacing h and scale gam for one dimension.
+// mlx_nufft/sizing.py:88-111
+void set_nhg_type3(double S, double X, double upsampfac, int w, int64_t* nf,
+                   double* h, double* gam) {
+    int nss = w + 1;
+    double Xsafe = X, Ssafe = S;
+    if (X == 0.0) {
+        if (S == 0.0) {
+            Xsafe = 1.0;
+            Ssafe = 1.0;
+        } else {
+            Xsafe = std::max(Xsafe, 1.0 / S);
+        }
+    } else {
+        Ssafe = std::max(Ssafe, 1.0 / X);
+    }
+    double nfd = 2.0 * upsampfac * Ssafe * Xsafe / kPi + nss;
+    int64_t n = (int64_t)nfd;
+    if (n < 2 * w) n = 2 * w;
+    n = next235even(n);
+    *nf = n;
+    *h = 2.0 * kPi / n;
+    *gam = n / (2.0 * upsampfac * Ssafe);
+}
+
+}  // namespace nufft

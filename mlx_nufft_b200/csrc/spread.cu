@@ -1,0 +1,132 @@
+// spread.cu -- launchers for the spreading kernels (types 1 and 3).
+#include <algorithm>
+#include <mutex>
+#include <set>
+
+#include "spreadinterp.cuh"
+
+namespace nufft {
+
+int tile_smem_limit() {
+    static int limit = 0;
+    if (!limit) {
+        int dev = 0, v = 0;
+        NUFFT_CUDA(cudaGetDevice(&dev));
+        NUFFT_CUDA(cudaDeviceGetAttribute(
+            &v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+        limit = v;
+    }
+    return limit;
+}
+
+void ensure_smem(const void* kernel, size_t bytes) {
+    static std::mutex mu;
+    static std::set<const void*> raised;
+    if (bytes <= 48 * 1024) return;
+    std::lock_guard<std::mutex> lk(mu);
+    if (raised.count(kernel)) return;
+    NUFFT_CUDA(cudaFuncSetAttribute(
+        kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tile_smem_limit()));
+    raised.insert(kernel);
+}
+
+namespace {
+
+template <int DIM, int W>
+void spread_impl(const PointSet& ps, const TileGeom& tg, const float2* c,
+                 int64_t cstride, int nvec, float2* grid, int nvg,
+                 cudaStream_t st) {
+    const uint32_t* perm = ps.sorted ? ps.perm : nullptr;
+    const CellPtrs cells = cell_ptrs(ps);
+    if (ps.tiled) {
+        if (ps.nsub == 0) return;
+        auto k = k_spread_tiled<DIM, W>;
+        for (int v0 = 0; v0 < nvec; v0 += nvg) {
+            const int nv = std::min(nvg, nvec - v0);
+            const size_t smem = (size_t)nv * tg.tcells * sizeof(float2);
+            ensure_smem((const void*)k, smem);
+            k<<<(unsigned)ps.nsub, 256, smem, st>>>(
+                c + v0 * cstride, cstride, nv, perm, cells, ps.phase, ps.subs,
+                grid + v0 * tg.ncells, tg);
+            NUFFT_LAUNCH("k_spread_tiled");
+        }
+    } else {
+        const unsigned blocks = (unsigned)((ps.M + 255) / 256);
+        k_spread_global<DIM, W><<<blocks, 256, 0, st>>>(
+            c, cstride, nvec, perm, cells, ps.phase, ps.M, grid, tg);
+        NUFFT_LAUNCH("k_spread_global");
+    }
+}
+
+// Disjoint-support spread: point j (sorted position) adds into grid
+// groups[caller index of j] only.
+template <int DIM, int W>
+__global__ void __launch_bounds__(256)
+k_spread_groups(const float2* __restrict__ c, const int32_t* __restrict__ groups,
+                const uint32_t* __restrict__ perm, CellPtrs cells, int64_t M,
+                float2* __restrict__ grid, TileGeom tg) {
+    const int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (j >= M) return;
+    const int64_t src = perm ? (int64_t)__ldg(perm + j) : j;
+    const int g = __ldg(groups + src);
+    if (g < 0) return;
+    float wgt[DIM][W];
+    int idx[DIM][W];
+    global_taps<DIM, W>(cells, j, tg, wgt, idx);
+    const float2 cv = __ldg(c + src);
+    float2* gv = grid + (int64_t)g * tg.ncells;
+    if (DIM == 1) {
+#pragma unroll
+        for (int a = 0; a < W; ++a)
+            atomicAdd(gv + idx[0][a], make_float2(cv.x * wgt[0][a], cv.y * wgt[0][a]));
+    } else if (DIM == 2) {
+#pragma unroll
+        for (int a = 0; a < W; ++a)
+#pragma unroll
+            for (int b = 0; b < W; ++b) {
+                const float wab = wgt[0][a] * wgt[DIM > 1 ? 1 : 0][b];
+                atomicAdd(gv + (int64_t)idx[0][a] * tg.n[1] + idx[DIM > 1 ? 1 : 0][b],
+                          make_float2(cv.x * wab, cv.y * wab));
+            }
+    } else {
+#pragma unroll 1
+        for (int a = 0; a < W; ++a)
+#pragma unroll
+            for (int b = 0; b < W; ++b) {
+                const float wab = wgt[0][a] * wgt[DIM > 1 ? 1 : 0][b];
+                const int64_t base =
+                    ((int64_t)idx[0][a] * tg.n[1] + idx[DIM > 1 ? 1 : 0][b]) *
+                    tg.n[DIM > 2 ? 2 : 0];
+#pragma unroll
+                for (int k = 0; k < W; ++k) {
+                    const float wk = wab * wgt[DIM > 2 ? 2 : 0][k];
+                    atomicAdd(gv + base + idx[DIM > 2 ? 2 : 0][k],
+                              make_float2(cv.x * wk, cv.y * wk));
+                }
+            }
+    }
+}
+
+}  // namespace
+
+void launch_spread(const PointSet& ps, const TileGeom& tg, int w,
+                   const float2* c, int64_t cstride, int nvec, float2* grid,
+                   int nvg, cudaStream_t st) {
+    NUFFT_DIM_SWITCH(ps.dim, NUFFT_WIDTH_SWITCH(w, spread_impl<DIM, W>(
+        ps, tg, c, cstride, nvec, grid, nvg, st)));
+}
+
+void launch_spread_groups(const PointSet& ps, const TileGeom& tg, int w,
+                          const float2* c, const int32_t* groups,
+                          float2* grid, cudaStream_t st) {
+    const uint32_t* perm = ps.sorted ? ps.perm : nullptr;
+    const CellPtrs cells = cell_ptrs(ps);
+    const unsigned blocks = (unsigned)((ps.M + 255) / 256);
+    NUFFT_DIM_SWITCH(ps.dim, NUFFT_WIDTH_SWITCH(w, {
+        k_spread_groups<DIM, W><<<blocks, 256, 0, st>>>(c, groups, perm, cells,
+                                                        ps.M, grid, tg);
+        NUFFT_LAUNCH("k_spread_groups");
+    }));
+}
+
+}  // namespace nufft

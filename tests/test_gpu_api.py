@@ -1,0 +1,251 @@
+"""GPU parity of the finufft-compatible API (mirrors the reference's
+harness/test_api_parity.py matrix, with the exact direct sum as the oracle
+instead of CPU finufft), the Plan interface, execute_adjoint, batched /
+re-pointed / disjoint type-1 execution (harness/test_type1_batch.py,
+harness/test_type1_setsources_gpu.py) and the error conventions."""
+
+import warnings
+
+import numpy as np
+import pytest
+
+from oracle import port, fast
+
+pytestmark = pytest.mark.gpu
+
+
+def gate(eps):
+    return max(10 * eps, 1e-5)
+
+
+M = 4000
+
+
+def pts(rng, dim, n=M):
+    return [rng.uniform(-np.pi, np.pi, n) for _ in range(dim)]
+
+
+@pytest.mark.parametrize("eps", [1e-3, 1e-5])
+@pytest.mark.parametrize("dim,N", [(1, (90,)), (1, (87,)), (2, (48, 36)),
+                                   (2, (45, 34)), (3, (24, 20, 16)),
+                                   (3, (21, 18, 14))])
+@pytest.mark.parametrize("isign", [+1, -1])
+def test_api_matrix(eps, dim, N, isign, rng):
+    import mlx_nufft_b200 as gpu
+    x = pts(rng, dim)
+    c = rng.standard_normal(M) + 1j * rng.standard_normal(M)
+    f1 = getattr(gpu, f"nufft{dim}d1")(*x, c, N, eps=eps, isign=isign)
+    assert f1.dtype == np.complex128 and f1.shape == N
+    assert port.rel_l2(f1, fast.direct_t1(x, c, N, isign).reshape(N)) <= gate(eps)
+    fk = rng.standard_normal(N) + 1j * rng.standard_normal(N)
+    c2 = getattr(gpu, f"nufft{dim}d2")(*x, fk, eps=eps, isign=isign)
+    assert c2.shape == (M,)
+    assert port.rel_l2(c2, fast.direct_t2(x, fk, isign)) <= gate(eps)
+    s = [rng.uniform(-30, 30, 1500) for _ in range(dim)]
+    f3 = getattr(gpu, f"nufft{dim}d3")(*x, c, *s, eps=eps, isign=isign)
+    assert f3.shape == (1500,)
+    assert port.rel_l2(f3, fast.direct_sum(x, c, s, isign)) <= gate(eps)
+
+
+def test_plan_interface_ntrans_c64_out(rng):
+    import mlx_nufft_b200 as gpu
+    eps = 1e-5
+    N = (40, 36)
+    x = pts(rng, 2)
+    cs = (rng.standard_normal((3, M)) + 1j * rng.standard_normal((3, M))
+          ).astype(np.complex64)
+    p = gpu.Plan(1, N, n_trans=3, eps=eps, isign=+1, dtype="complex64")
+    p.setpts(*x)
+    out = np.empty((3,) + N, dtype=np.complex64)
+    got = p.execute(cs, out=out)
+    assert got is out and out.dtype == np.complex64
+    for b in range(3):
+        ref = fast.direct_t1(x, cs[b], N, +1).reshape(N)
+        assert port.rel_l2(out[b], ref) <= gate(eps)
+    p2 = gpu.Plan(2, N, n_trans=3, eps=eps, isign=-1, dtype="complex64")
+    p2.setpts(*x)
+    fks = (rng.standard_normal((3,) + N) + 1j * rng.standard_normal((3,) + N)
+           ).astype(np.complex64)
+    got2 = p2.execute(fks)
+    for b in range(3):
+        assert port.rel_l2(got2[b], fast.direct_t2(x, fks[b], -1)) <= gate(eps)
+    p3 = gpu.Plan(3, 2, n_trans=1, eps=eps, isign=+1)
+    s = [rng.uniform(-30, 30, 1500) for _ in range(2)]
+    p3.setpts(x[0], x[1], s=s[0], t=s[1])
+    c = rng.standard_normal(M) + 1j * rng.standard_normal(M)
+    assert port.rel_l2(p3.execute(c), fast.direct_sum(x, c, s, +1)) <= gate(eps)
+    with pytest.raises(ValueError):
+        p.execute(cs[:2])
+
+
+def test_execute_adjoint(rng):
+    import mlx_nufft_b200 as gpu
+    N = (30, 22)
+    x = pts(rng, 2)
+    p = gpu.Plan(1, N, eps=1e-6, isign=+1)
+    p.setpts(*x)
+    fk = rng.standard_normal(N) + 1j * rng.standard_normal(N)
+    adj = p.execute_adjoint(fk)          # type 2 with isign -1
+    assert port.rel_l2(adj, fast.direct_t2(x, fk, -1)) <= gate(1e-6)
+    q = gpu.Plan(2, N, eps=1e-6)
+    q.setpts(*x)
+    c = rng.standard_normal(M) + 1j * rng.standard_normal(M)
+    adj2 = q.execute_adjoint(c)          # type 1 with isign +1
+    assert port.rel_l2(adj2, fast.direct_t1(x, c, N, +1).reshape(N)) <= gate(1e-6)
+    r = gpu.Plan(3, 1, eps=1e-6)
+    s = rng.uniform(-20, 20, 900)
+    r.setpts(x[0], s=s)
+    g = rng.standard_normal(900) + 1j * rng.standard_normal(900)
+    adj3 = r.execute_adjoint(g)          # targets -> sources, isign -1
+    assert port.rel_l2(adj3, fast.direct_sum([s], g, [x[0]], -1)) <= gate(1e-6)
+
+
+def test_adjoint_pairing_3d(rng):
+    """<T1 c, f> == <c, T2 f> (harness/test_types12.py:40-48)."""
+    from mlx_nufft_b200 import Type1Plan, Type2Plan
+    N = (32, 24, 16)
+    x = pts(rng, 3, 50_000)
+    c = rng.standard_normal(50_000) + 1j * rng.standard_normal(50_000)
+    fk = rng.standard_normal(N) + 1j * rng.standard_normal(N)
+    f1 = Type1Plan(x, N, eps=1e-5, isign=+1).execute(c.astype(np.complex64))
+    c2 = Type2Plan(x, N, eps=1e-5, isign=-1).execute(fk.astype(np.complex64))
+    lhs = np.vdot(fk, f1)
+    rhs = np.vdot(c2, c)
+    assert abs(lhs - rhs) / abs(lhs) < 1e-5
+    with pytest.raises(AssertionError):
+        Type1Plan(x, (31, 24, 16))
+
+
+def test_dtype_roundtrip_and_options(rng):
+    import mlx_nufft_b200 as gpu
+    x = pts(rng, 1)
+    c = (rng.standard_normal(M) + 1j * rng.standard_normal(M)).astype(np.complex64)
+    assert gpu.nufft1d1(x[0], c, 16).dtype == np.complex64
+    assert gpu.nufft1d1(x[0], c.astype(np.complex128), 16).dtype == np.complex128
+    with pytest.raises(NotImplementedError):
+        gpu.nufft1d1(x[0], c, 16, modeord=1)
+    with warnings.catch_warnings(record=True) as w:
+        warnings.simplefilter("always")
+        gpu.nufft1d1(x[0], c, 16, eps=1e-9)
+        gpu.nufft1d1(x[0], c, 16, foo=3, nthreads=4)
+    msgs = " ".join(str(v.message) for v in w)
+    assert "clamping" in msgs and "foo" in msgs and "nthreads" not in msgs
+    out = np.empty(16, dtype=np.complex128)
+    assert gpu.nufft1d1(x[0], c, out=out) is out
+    cs = np.stack([c, c])
+    f2 = gpu.nufft1d1(x[0], cs, 16)
+    assert f2.shape == (2, 16)
+    with pytest.raises(ValueError):
+        gpu.nufft1d1(x[0], c[:10], 16)
+    with pytest.raises(ValueError):
+        gpu.Plan(4, (8,))
+    with pytest.raises(ValueError):
+        gpu.Plan(1, (8,), dtype="float32")
+    with pytest.raises(RuntimeError):
+        gpu.Plan(1, (8,)).execute(c)
+
+
+def test_torch_inputs_and_device_outputs(rng):
+    import torch
+    from mlx_nufft_b200 import Type1PlanND, Type2PlanND
+    x = torch.from_numpy(rng.uniform(-np.pi, np.pi, M)).cuda()
+    c = torch.randn(M, dtype=torch.complex64, device="cuda")
+    p = Type1PlanND(x, (64,), eps=1e-6)
+    f = p.execute(c, return_np=False)
+    assert isinstance(f, torch.Tensor) and f.is_cuda and f.shape == (64,)
+    ref = fast.direct_t1([x.cpu().numpy()], c.cpu().numpy(), (64,), +1)
+    assert port.rel_l2(f.cpu().numpy(), ref) <= gate(1e-6)
+    q = Type2PlanND(x.cpu(), (64,), eps=1e-6)
+    cj = q.execute(f, return_np=False)
+    assert cj.is_cuda and cj.shape == (M,)
+
+
+# ---------------------------------------------------- batch / re-point
+@pytest.mark.parametrize("dim,N,P,B", [(1, (4096,), 200_000, 5),
+                                       (2, (256, 256), 200_000, 5),
+                                       (2, (192, 160), 5_000, 4),
+                                       (3, (64, 64, 48), 5_000, 6),
+                                       (3, (64, 64, 48), 200_000, 8)])
+@pytest.mark.parametrize("isign", [+1, -1])
+def test_execute_batch(dim, N, P, B, isign, rng):
+    from mlx_nufft_b200 import Type1PlanND
+    x = pts(rng, dim, P)
+    cs = (rng.standard_normal((B, P)) + 1j * rng.standard_normal((B, P))
+          ).astype(np.complex64)
+    plan = Type1PlanND(tuple(x), N, eps=1e-5, isign=isign)
+    fb = plan.execute_batch(cs)
+    assert fb.shape == (B,) + N
+    idx = rng.choice(int(np.prod(N)), 100, replace=False)
+    for b in range(B):
+        fl = plan.execute(cs[b])
+        assert port.rel_l2(fb[b], fl) < 1e-5                    # batch == loop
+        ref = fast.direct_t1(x, cs[b], N, isign, idx)
+        assert port.rel_l2(fb[b].ravel()[idx], ref) <= gate(1e-5)
+
+
+@pytest.mark.parametrize("dim,N,P", [(2, (256, 256), 50_000),
+                                     (3, (64, 64, 48), 50_000)])
+def test_set_sources_repoint(dim, N, P, rng):
+    from mlx_nufft_b200 import Type1PlanND
+    x1, x2 = pts(rng, dim, P), pts(rng, dim, P)
+    c = (rng.standard_normal(P) + 1j * rng.standard_normal(P)).astype(np.complex64)
+    plan = Type1PlanND(tuple(x1), N, eps=1e-5, isign=+1)
+    for backend in ("host", "gpu"):
+        plan.set_sources(x2, backend=backend)
+        fresh = Type1PlanND(tuple(x2), N, eps=1e-5, isign=+1).execute(c)
+        assert port.rel_l2(plan.execute(c), fresh) < 1e-5
+    P2 = P // 3
+    x3 = pts(rng, dim, P2)
+    c3 = c[:P2]
+    plan.set_sources(x3)
+    assert plan.P == P2
+    fresh = Type1PlanND(tuple(x3), N, eps=1e-5, isign=+1).execute(c3)
+    assert port.rel_l2(plan.execute(c3), fresh) < 1e-5
+    with pytest.raises(ValueError):
+        plan.set_sources(x3, backend="cuda")
+
+
+def test_execute_disjoint(rng):
+    from mlx_nufft_b200 import Type1PlanND
+    P, N, G = 100_000, (128, 96), 4
+    x = pts(rng, 2, P)
+    c = (rng.standard_normal(P) + 1j * rng.standard_normal(P)).astype(np.complex64)
+    groups = rng.integers(0, G, P)
+    plan = Type1PlanND(tuple(x), N, eps=1e-5)
+    fd = plan.execute_disjoint(c, groups)
+    assert fd.shape == (G,) + N
+    for g in range(G):
+        sub = np.where(groups == g, c, 0)
+        assert port.rel_l2(fd[g], plan.execute(sub)) < 1e-5
+    with pytest.raises(ValueError):
+        plan.execute_disjoint(c, groups[:10])
+
+
+def test_error_conventions(rng):
+    from mlx_nufft_b200 import Type1PlanND, Type2PlanND, Type3Plan
+    x = pts(rng, 2, 1000)
+    with pytest.raises(ValueError):
+        Type1PlanND(tuple(x), (16, 16, 16))
+    with pytest.raises(ValueError):
+        Type1PlanND(tuple(x), (16, 0))
+    with pytest.raises(ValueError):
+        Type1PlanND(tuple(x), (16, 16), upsampfac=5.0)
+    with pytest.raises(ValueError):
+        Type1PlanND(tuple(x), (16, 16), prec="fp16")
+    with pytest.raises(ValueError):
+        Type1PlanND((x[0], x[1][:10]), (16, 16))
+    p = Type1PlanND(tuple(x), (16, 16))
+    with pytest.raises(ValueError):
+        p.execute(np.zeros(999, np.complex64))
+    q = Type2PlanND(tuple(x), (16, 16))
+    with pytest.raises(ValueError):
+        q.execute(np.zeros((16, 15), np.complex64))
+    with pytest.raises(ValueError):
+        Type1PlanND((np.array([0.0, np.nan]),), (8,))
+    with pytest.raises(AssertionError):
+        Type3Plan(tuple(x), tuple(x), prec="bad")
+    with pytest.raises(RuntimeError):
+        Type3Plan(tuple(x), tuple(x), fft_backend="vkfft")
+    t3 = Type3Plan(tuple(x), tuple(x))
+    with pytest.raises(AssertionError):
+        t3.execute(np.zeros(5, np.complex64))

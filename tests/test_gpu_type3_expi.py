@@ -1,0 +1,164 @@
+"""GPU parity: type 3 against the reference's own CPU type-3 plan
+(mlx_nufft/ref_t3.py run in the build container -> tests/golden/t3_ref.npz)
+and the exact direct sum; expi against the fp64 host reference with the
+reference's gates (harness/test_expi.py:26-27)."""
+
+import numpy as np
+import pytest
+
+from oracle import port, fast
+
+pytestmark = pytest.mark.gpu
+
+
+def gate(eps):
+    return max(10 * eps, 1e-5)
+
+
+@pytest.mark.parametrize("case", [0, 1, 2])
+def test_type3_vs_ref_t3_golden(golden, case):
+    from mlx_nufft_b200 import Type3Plan
+    g = golden("t3_ref")
+    p = f"c{case}_"
+    eps = float(g[p + "eps"])
+    plan = Type3Plan(tuple(g[p + "x"]), tuple(g[p + "s"]), eps=eps,
+                     isign=int(g[p + "isign"]))
+    # plan geometry identical to the reference's
+    assert plan.nf == list(g[p + "nf"]) and plan.n_up == list(g[p + "n_up"])
+    assert plan.w == g[p + "w"] and plan.beta == g[p + "beta"]
+    np.testing.assert_array_equal(plan.C, g[p + "C"])
+    np.testing.assert_array_equal(plan.D, g[p + "D"])
+    np.testing.assert_array_equal(plan.gam, g[p + "gam"])
+    # device cells == the reference's fp64 cells (fr rounded to fp32)
+    i1, fr, perm = plan.cells(0)
+    for d in range(3):
+        np.testing.assert_array_equal(
+            i1[d], port.normalize_cells(g[p + "i1"][d][perm], plan.nf[d], plan.w))
+        np.testing.assert_array_equal(fr[d], g[p + "fr"][d][perm].astype(np.float32))
+    ti1, tfr, tperm = plan.cells(1)
+    for d in range(3):
+        np.testing.assert_array_equal(
+            ti1[d], port.normalize_cells(g[p + "t_i1"][d][tperm], plan.n_up[d],
+                                         plan.w))
+        np.testing.assert_array_equal(tfr[d],
+                                      g[p + "t_fr"][d][tperm].astype(np.float32))
+    f = plan.execute(g[p + "c"])
+    assert port.rel_l2(f, g[p + "out"]) <= 2e-5
+    assert port.rel_l2(f, g[p + "direct"]) <= gate(eps)
+
+
+@pytest.mark.parametrize("dim", [1, 2, 3])
+@pytest.mark.parametrize("isign", [+1, -1])
+@pytest.mark.parametrize("eps", [1e-3, 1e-5, 1e-6])
+def test_type3_dims_vs_direct(dim, isign, eps, rng):
+    from mlx_nufft_b200 import Type3Plan
+    P, M = 4000, 1500
+    x = [rng.uniform(-np.pi, np.pi, P) for _ in range(dim)]
+    s = [rng.uniform(-30, 30, M) for _ in range(dim)]
+    c = rng.standard_normal(P) + 1j * rng.standard_normal(P)
+    f = Type3Plan(tuple(x), tuple(s), eps=eps, isign=isign).execute(c)
+    assert port.rel_l2(f, fast.direct_sum(x, c, s, isign)) <= gate(eps)
+    ref = port.nufft_t3(x, c, s, eps=eps, isign=isign)
+    assert port.rel_l2(f, ref) <= 2e-5
+
+
+def test_type3_tiled_large(rng):
+    from mlx_nufft_b200 import Type3Plan
+    P, M = 300_000, 250_000
+    x = [rng.uniform(-10, 10, P) for _ in range(3)]
+    s = [rng.uniform(-20, 20, M) for _ in range(3)]
+    c = rng.standard_normal(P) + 1j * rng.standard_normal(P)
+    plan = Type3Plan(tuple(x), tuple(s), eps=1e-5)
+    assert plan._plan.info().tiled
+    f = plan.execute(c)
+    idx = rng.choice(M, 200, replace=False)
+    assert port.rel_l2(f[idx], fast.direct_sum(x, c, s, +1, idx)) <= gate(1e-5)
+
+
+def test_type3_adjoint_identity(rng):
+    """gpu t3 adjoint: swap roles and negate isign (test_gpu_small.py:40-46):
+    <T c, g> == <c, T^H g>."""
+    from mlx_nufft_b200 import Type3Plan
+    x = [rng.uniform(-4, 4, 3000) for _ in range(3)]
+    s = [rng.uniform(-6, 6, 2000) for _ in range(3)]
+    c = rng.standard_normal(3000) + 1j * rng.standard_normal(3000)
+    g = rng.standard_normal(2000) + 1j * rng.standard_normal(2000)
+    Tc = Type3Plan(tuple(x), tuple(s), eps=1e-6, isign=+1).execute(c)
+    Tg = Type3Plan(tuple(s), tuple(x), eps=1e-6, isign=-1).execute(g)
+    lhs = np.vdot(g, Tc)
+    rhs = np.vdot(Tg, c)
+    assert abs(lhs - rhs) / abs(lhs) < 1e-5
+
+
+def test_type3_set_sources_and_guard(rng):
+    from mlx_nufft_b200 import Type3Plan
+    x = [rng.uniform(-5, 5, 5000) for _ in range(3)]
+    s = [rng.uniform(-8, 8, 2000) for _ in range(3)]
+    c = rng.standard_normal(5000) + 1j * rng.standard_normal(5000)
+    plan = Type3Plan(tuple(x), tuple(s), eps=1e-5,
+                     source_extent=[(-5, 5)] * 3)
+    x2 = [rng.uniform(-5, 5, 4000) for _ in range(3)]
+    c2 = c[:4000]
+    plan.set_sources(x2)
+    f = plan.execute(c2)
+    assert port.rel_l2(f, fast.direct_sum(x2, c2, s, +1)) <= gate(1e-5)
+    with pytest.raises(ValueError, match="exceed"):
+        plan.set_sources([v * 3.0 for v in x2])
+    with pytest.raises(ValueError):
+        plan.set_sources(x2, backend="cuda")
+
+
+def test_type3_batch_equals_loop(rng):
+    from mlx_nufft_b200 import Type3Plan
+    x = [rng.uniform(-3, 3, 30_000) for _ in range(3)]
+    s = [rng.uniform(-7, 7, 25_000) for _ in range(3)]
+    cs = (rng.standard_normal((3, 30_000)) +
+          1j * rng.standard_normal((3, 30_000))).astype(np.complex64)
+    plan = Type3Plan(tuple(x), tuple(s), eps=1e-5)
+    fb = plan.execute_batch(cs)
+    for b in range(3):
+        assert port.rel_l2(fb[b], plan.execute(cs[b])) < 1e-5
+
+
+# ---------------------------------------------------------------- expi
+GATE_1E8 = 3e-6
+GATE_SMALL = 5e-7
+
+
+@pytest.mark.parametrize("mag,gate_", [(1e0, GATE_SMALL), (1e3, GATE_SMALL),
+                                       (1e5, GATE_SMALL), (1e6, GATE_SMALL),
+                                       (1e7, GATE_SMALL), (5e7, GATE_1E8),
+                                       (1e8, GATE_1E8)])
+def test_expi_magnitude_sweep(mag, gate_, rng):
+    from mlx_nufft_b200 import expi
+    phi = rng.uniform(-mag, mag, 200_000)
+    e = expi(phi, return_np=True)
+    assert np.max(np.abs(e - port.expi_ref(phi))) <= gate_
+
+
+def test_expi_isign_components_shape(rng):
+    import torch
+    from mlx_nufft_b200 import expi, EXPI_MAX_PHASE
+    assert abs(EXPI_MAX_PHASE - 2 ** 24 * 2 * np.pi) < 1e-6
+    phi = rng.uniform(-1e8, 1e8, 200_000)
+    for isign in (+1, -1):
+        e = expi(phi, isign=isign, return_np=True)
+        assert np.max(np.abs(e - port.expi_ref(phi, isign))) <= GATE_1E8
+    comps = [rng.uniform(-3.3e7, 3.3e7, 200_000) for _ in range(3)]
+    e = expi(comps, return_np=True)
+    ref = np.exp(1j * sum(comps))
+    assert np.max(np.abs(e - ref)) <= GATE_1E8
+    one = rng.uniform(-1e8, 1e8, 5000)
+    assert np.array_equal(expi([one], return_np=True), expi(one, return_np=True))
+    with pytest.raises(ValueError):
+        expi([0.3, 1.7, -2.2])
+    phi2 = rng.uniform(-1e8, 1e8, (128, 97))
+    dev = expi(phi2)
+    assert isinstance(dev, torch.Tensor) and dev.is_cuda
+    assert dev.dtype == torch.complex64 and tuple(dev.shape) == (128, 97)
+    assert np.max(np.abs(dev.cpu().numpy() - np.exp(1j * phi2))) <= GATE_1E8
+    bad = expi(np.array([np.nan, np.inf, -np.inf, 1.0]), return_np=True)
+    assert np.all(np.isnan(bad[:3])) and np.isfinite(bad[3])
+    # beyond the reference's ceiling the fp64 reduction stays accurate
+    big = rng.uniform(-1e9, 1e9, 50_000)
+    assert np.max(np.abs(expi(big, return_np=True) - np.exp(1j * big))) < 1e-5
