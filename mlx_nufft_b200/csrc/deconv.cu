@@ -78,14 +78,16 @@ k_crop(const float2* __restrict__ grid, float2* __restrict__ fk, DecPtrs dec,
 // Pad: H[v][r] = f[v][m(r)] * prod dec if every dim is in band, else 0.
 // In-band test (nd.py:894-901): q = r - n if r >= n - N/2; band is
 // -N/2 <= q < N - N/2; m = q + N/2.
+// Each thread writes two consecutive fine cells with one 16-byte store
+// (fine-grid extents are even, so rows stay 16-byte aligned).
 __global__ void __launch_bounds__(256)
 k_pad(const float2* __restrict__ f, float2* __restrict__ H, DecPtrs dec,
       BoxGrid bg, int chunks_per_row) {
     const int dim = bg.dim;
     const int L = dim - 1;
     const int64_t row = blockIdx.x / chunks_per_row;
-    const int r_in = (int)(blockIdx.x % chunks_per_row) * blockDim.x + threadIdx.x;
-    if (r_in >= bg.n[L]) return;
+    const int r0 = 2 * ((int)(blockIdx.x % chunks_per_row) * blockDim.x + threadIdx.x);
+    if (r0 >= bg.n[L]) return;
     const int v = blockIdx.y;
     int r[3] = {0, 0, 0};
     split_row(row, bg.n, dim, r);
@@ -102,16 +104,25 @@ k_pad(const float2* __restrict__ f, float2* __restrict__ H, DecPtrs dec,
             dout = (d == 0) ? dec.d[0][md] : dout * dec.d[d][md];
         }
     }
-    int q = r_in;
-    if (q >= bg.n[L] - bg.N[L] / 2) q -= bg.n[L];
-    const int mi = q + bg.N[L] / 2;
-    float2 out = make_float2(0.0f, 0.0f);
-    if (inband && mi >= 0 && mi < bg.N[L]) {
-        const float dd = (L == 0) ? dec.d[0][mi] : dout * dec.d[L][mi];
-        const float2 g = f[v * bg.K + mrow * bg.N[L] + mi];
-        out = make_float2(g.x * dd, g.y * dd);
+    float4 out = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (inband) {
+        const float2* frow = f + v * bg.K + mrow * bg.N[L];
+        const int lo = bg.n[L] - bg.N[L] / 2;     // first negative-mode cell
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            int q = r0 + e;
+            if (q >= lo) q -= bg.n[L];
+            const int mi = q + bg.N[L] / 2;
+            if (mi >= 0 && mi < bg.N[L]) {
+                const float dd = (L == 0) ? __ldg(dec.d[0] + mi)
+                                          : dout * __ldg(dec.d[L] + mi);
+                const float2 g = __ldg(frow + mi);
+                if (e == 0) { out.x = g.x * dd; out.y = g.y * dd; }
+                else        { out.z = g.x * dd; out.w = g.y * dd; }
+            }
+        }
     }
-    H[v * bg.ncells + row * bg.n[L] + r_in] = out;
+    *reinterpret_cast<float4*>(H + v * bg.ncells + row * bg.n[L] + r0) = out;
 }
 
 namespace {
@@ -163,7 +174,8 @@ void launch_pad(int dim, const int64_t* N, const int64_t* n,
                 cudaStream_t st) {
     const BoxGrid bg = make_boxgrid(dim, N, n);
     const int inner = bg.n[dim - 1];
-    const int cpr = (inner + 255) / 256;
+    if (inner % 2) fail(-1, "fine-grid extents must be even");
+    const int cpr = (inner / 2 + 255) / 256;
     const int64_t rows = bg.ncells / inner;
     const int64_t blocks = rows * cpr;
     if (blocks > 0x7fffffffLL) fail(-1, "fine grid too large");

@@ -41,6 +41,21 @@ void kernel_ft_nodes(double beta, int w, std::vector<double>* d,
 double kernel_ft(double xi, double beta, int w);
 void set_nhg_type3(double S, double X, double upsampfac, int w, int64_t* nf,
                    double* h, double* gam);
+// Monomial coefficients coef[k * w + l] (k = 0..deg) of the per-tap
+// polynomials psi(l - fr) = sum_k coef[k][l] t^k, t = fr - (w/2 - 1/2).
+void es_poly_coeffs(int w, double beta, int deg, float* coef);
+
+// Kernel-width limits and the polynomial degree used for width W.
+constexpr int kMaxW = 16;
+constexpr int kMaxDeg = kMaxW + 2;
+__host__ __device__ constexpr int es_degree(int w) { return w + 2; }
+
+// ES kernel polynomial coefficients, passed to the kernels by value so that
+// every coefficient is a constant-bank operand of its FFMA.
+struct EsPoly {
+    float c[kMaxDeg + 1][kMaxW];
+};
+EsPoly make_es_poly(int w, double beta);
 
 // ---------------------------------------------------------------------
 // geometry handed to the device kernels by value.
@@ -79,6 +94,7 @@ struct TileGeom {
     int halfw;            // w / 2
     float c2w;            // (float)(2.0 / w)
     float beta;           // (float) beta
+    EsPoly poly;          // ES kernel as per-tap polynomials in fr
 };
 
 // One sorted (or caller-ordered) set of nonuniform points on the device.
@@ -92,9 +108,14 @@ struct PointSet {
     int64_t cap = 0;            // allocated points
     int64_t subcap = 0;         // allocated subproblems
     float2* phase = nullptr;    // type 3: prephase / postphase, sorted order
+    int* sched = nullptr;       // 2 ints: dynamic subproblem scheduler state
     bool sorted = false;
     bool tiled = false;
 };
+
+// CTAs for a persistent launch of `kernel` (256 threads, `smem` bytes):
+// resident CTAs per SM x SMs, capped at `work` items.
+int persistent_grid(const void* kernel, size_t smem, int64_t work);
 
 // ---------------------------------------------------------------------
 // device memory helpers

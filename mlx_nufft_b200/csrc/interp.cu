@@ -20,9 +20,10 @@ void interp_impl(const PointSet& ps, const TileGeom& tg, const float2* grid,
             const int nv = std::min(nvg, nvec - v0);
             const size_t smem = (size_t)nv * tg.tcells * sizeof(float2);
             ensure_smem((const void*)k, smem);
-            k<<<(unsigned)ps.nsub, 256, smem, st>>>(
+            const int blocks = persistent_grid((const void*)k, smem, ps.nsub);
+            k<<<blocks, 256, smem, st>>>(
                 grid + v0 * tg.ncells, nv, perm, cells, ps.phase, ps.subs,
-                out + v0 * ostride, ostride, tg);
+                (int)ps.nsub, ps.sched, out + v0 * ostride, ostride, tg);
             NUFFT_LAUNCH("k_interp_tiled");
         }
     } else {

@@ -157,6 +157,7 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta) {
     tg.halfw = w / 2;
     tg.c2w = (float)(2.0 / w);
     tg.beta = (float)beta;
+    tg.poly = make_es_poly(w, beta);
     int m0 = dim == 1 ? 1024 : (dim == 2 ? 32 : 8);
     for (int d = 0; d < 3; ++d) {
         if (d < dim) {

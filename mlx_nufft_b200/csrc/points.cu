@@ -313,9 +313,11 @@ void free_pointset(PointSet* ps) {
     dfree(ps->perm);
     dfree(ps->subs);
     dfree(ps->phase);
+    dfree(ps->sched);
     ps->perm = nullptr;
     ps->subs = nullptr;
     ps->phase = nullptr;
+    ps->sched = nullptr;
     ps->cap = ps->subcap = ps->M = ps->nsub = 0;
 }
 
@@ -409,6 +411,8 @@ void build_pointset(PointSet* ps, const CellParams& cp, int64_t M,
             ps->cell[d] = (int2*)dmalloc(sizeof(int2) * M, "point cells");
         ps->perm = (uint32_t*)dmalloc(4 * M, "point permutation");
         if (pp.mode) ps->phase = (float2*)dmalloc(sizeof(float2) * M, "phases");
+        ps->sched = (int*)dmalloc(2 * sizeof(int), "scheduler");
+        NUFFT_CUDA(cudaMemsetAsync(ps->sched, 0, 2 * sizeof(int), st));
         ps->cap = M;
     }
     ps->dim = cp.dim;

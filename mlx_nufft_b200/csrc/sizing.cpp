@@ -118,6 +118,68 @@ double kernel_ft(double xi, double beta, int w) {
     return 2.0 * s;
 }
 
+// Piecewise-polynomial form of the ES kernel used by the device kernels
+// (the "Horner" evaluation of FINUFFT, Barnett, Magland & af Klinteberg,
+// SIAM J. Sci. Comput. 41 (2019)): for a point with fraction fr in
+// (w/2 - 1, w/2], tap l has weight psi(l - fr) = sum_k c[k][l] t^k with
+// t = fr - (w/2 - 1/2) in (-1/2, 1/2].  Each tap's polynomial is the
+// degree-`deg` interpolant at Chebyshev nodes of [-1/2, 1/2], computed in
+// fp64 and converted to the monomial basis.  Its error is at the level of
+// the kernel's edge value exp(-beta) (~3e-8 for w = 7), below the kernel's
+// own truncation error.
+void es_poly_coeffs(int w, double beta, int deg, float* coef) {
+    const int n = deg + 1;
+    std::vector<double> s(n), a(n), mono(n), Tm1(n), T(n), Tn(n);
+    for (int i = 0; i < n; ++i) s[i] = std::cos(kPi * (i + 0.5) / n);
+    for (int l = 0; l < w; ++l) {
+        // Chebyshev coefficients of y(s) = psi(l - (w/2 - 1/2) - s/2)
+        for (int j = 0; j < n; ++j) {
+            double acc = 0.0;
+            for (int i = 0; i < n; ++i) {
+                const double d = l - (w / 2.0 - 0.5) - 0.5 * s[i];
+                acc += es_kernel64(d, beta, w) * std::cos(j * kPi * (i + 0.5) / n);
+            }
+            a[j] = 2.0 / n * acc;
+        }
+        a[0] *= 0.5;
+        // sum_j a_j T_j(s) in the monomial basis of s
+        std::fill(mono.begin(), mono.end(), 0.0);
+        std::fill(Tm1.begin(), Tm1.end(), 0.0);
+        std::fill(T.begin(), T.end(), 0.0);
+        Tm1[0] = 1.0;
+        mono[0] = a[0];
+        if (n > 1) {
+            T[1] = 1.0;
+            mono[1] += a[1];
+        }
+        for (int j = 2; j < n; ++j) {
+            std::fill(Tn.begin(), Tn.end(), 0.0);
+            for (int k = 0; k + 1 < n; ++k) Tn[k + 1] = 2.0 * T[k];
+            for (int k = 0; k < n; ++k) Tn[k] -= Tm1[k];
+            for (int k = 0; k < n; ++k) mono[k] += a[j] * Tn[k];
+            Tm1.swap(T);
+            T.swap(Tn);
+        }
+        // s = 2t
+        double scale = 1.0;
+        for (int k = 0; k < n; ++k) {
+            coef[k * w + l] = (float)(mono[k] * scale);
+            scale *= 2.0;
+        }
+    }
+}
+
+EsPoly make_es_poly(int w, double beta) {
+    EsPoly p{};
+    if (w < 2 || w > kMaxW) return p;
+    const int deg = es_degree(w);
+    std::vector<float> c((size_t)(deg + 1) * w);
+    es_poly_coeffs(w, beta, deg, c.data());
+    for (int k = 0; k <= deg; ++k)
+        for (int l = 0; l < w; ++l) p.c[k][l] = c[(size_t)k * w + l];
+    return p;
+}
+
 // Type-3 spread-grid size nf, spacing h and scale gam for one dimension.
 // mlx_nufft/sizing.py:88-111
 void set_nhg_type3(double S, double X, double upsampfac, int w, int64_t* nf,

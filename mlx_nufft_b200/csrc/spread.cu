@@ -1,7 +1,9 @@
 // spread.cu -- launchers for the spreading kernels (types 1 and 3).
 #include <algorithm>
+#include <map>
 #include <mutex>
 #include <set>
+#include <utility>
 
 #include "spreadinterp.cuh"
 
@@ -17,6 +19,32 @@ int tile_smem_limit() {
         limit = v;
     }
     return limit;
+}
+
+int persistent_grid(const void* kernel, size_t smem, int64_t work) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, size_t>, int> cache;
+    static int sms = 0;
+    int per_sm = 0;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!sms) {
+            int dev = 0;
+            NUFFT_CUDA(cudaGetDevice(&dev));
+            NUFFT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        }
+        auto key = std::make_pair(kernel, smem);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            per_sm = it->second;
+        } else {
+            NUFFT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel,
+                                                                     256, smem));
+            per_sm = std::max(per_sm, 1);
+            cache[key] = per_sm;
+        }
+    }
+    return (int)std::max<int64_t>(1, std::min<int64_t>(work, (int64_t)per_sm * sms));
 }
 
 void ensure_smem(const void* kernel, size_t bytes) {
@@ -45,9 +73,10 @@ void spread_impl(const PointSet& ps, const TileGeom& tg, const float2* c,
             const int nv = std::min(nvg, nvec - v0);
             const size_t smem = (size_t)nv * tg.tcells * sizeof(float2);
             ensure_smem((const void*)k, smem);
-            k<<<(unsigned)ps.nsub, 256, smem, st>>>(
+            const int blocks = persistent_grid((const void*)k, smem, ps.nsub);
+            k<<<blocks, 256, smem, st>>>(
                 c + v0 * cstride, cstride, nv, perm, cells, ps.phase, ps.subs,
-                grid + v0 * tg.ncells, tg);
+                (int)ps.nsub, ps.sched, grid + v0 * tg.ncells, tg);
             NUFFT_LAUNCH("k_spread_tiled");
         }
     } else {
@@ -73,38 +102,8 @@ k_spread_groups(const float2* __restrict__ c, const int32_t* __restrict__ groups
     float wgt[DIM][W];
     int idx[DIM][W];
     global_taps<DIM, W>(cells, j, tg, wgt, idx);
-    const float2 cv = __ldg(c + src);
-    float2* gv = grid + (int64_t)g * tg.ncells;
-    if (DIM == 1) {
-#pragma unroll
-        for (int a = 0; a < W; ++a)
-            atomicAdd(gv + idx[0][a], make_float2(cv.x * wgt[0][a], cv.y * wgt[0][a]));
-    } else if (DIM == 2) {
-#pragma unroll
-        for (int a = 0; a < W; ++a)
-#pragma unroll
-            for (int b = 0; b < W; ++b) {
-                const float wab = wgt[0][a] * wgt[DIM > 1 ? 1 : 0][b];
-                atomicAdd(gv + (int64_t)idx[0][a] * tg.n[1] + idx[DIM > 1 ? 1 : 0][b],
-                          make_float2(cv.x * wab, cv.y * wab));
-            }
-    } else {
-#pragma unroll 1
-        for (int a = 0; a < W; ++a)
-#pragma unroll
-            for (int b = 0; b < W; ++b) {
-                const float wab = wgt[0][a] * wgt[DIM > 1 ? 1 : 0][b];
-                const int64_t base =
-                    ((int64_t)idx[0][a] * tg.n[1] + idx[DIM > 1 ? 1 : 0][b]) *
-                    tg.n[DIM > 2 ? 2 : 0];
-#pragma unroll
-                for (int k = 0; k < W; ++k) {
-                    const float wk = wab * wgt[DIM > 2 ? 2 : 0][k];
-                    atomicAdd(gv + base + idx[DIM > 2 ? 2 : 0][k],
-                              make_float2(cv.x * wk, cv.y * wk));
-                }
-            }
-    }
+    global_add<DIM, W>(grid + (int64_t)g * tg.ncells, tg, wgt, idx,
+                       __ldg(c + src));
 }
 
 }  // namespace

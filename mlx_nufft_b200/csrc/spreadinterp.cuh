@@ -13,9 +13,16 @@
 //    per point reading / atomically updating the fine grid directly; used
 //    for small point counts and when the grid is L2-resident.
 //
-// The ES kernel psi(d) = exp(beta (sqrt(1 - (2d/w)^2) - 1)) is evaluated in
-// fp32 with the accurate expf/sqrtf (no fast-math), as the reference does
-// with metal::precise (mlx_nufft/gpu_t3.py:30-37).
+// Kernel weights: the reference evaluates psi(d) = exp(beta (sqrt(1 -
+// (2d/w)^2) - 1)) with fp32 exp/sqrt per tap (mlx_nufft/gpu_t3.py:30-37).
+// Here the W weights of a point come from per-tap polynomials in the
+// point's fraction (es_weights, coefficients fitted in fp64 at plan time,
+// sizing.cpp es_poly_coeffs): W*(W+2) FMAs with constant-bank operands,
+// within ~1e-7 of the exact kernel.
+//
+// The x-weights of 3-D loops live in registers and are rotated once per
+// rolled outer iteration, so no weight array is ever indexed dynamically
+// (no local-memory stack frame).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -28,10 +35,35 @@ struct CellPtrs {
     const int2* d[3];
 };
 
+// Exact ES kernel in fp32 (reference form, kept for checks).
 __device__ __forceinline__ float es_weight(float d, float c2w, float beta) {
     float z = d * c2w;
     float t = fmaxf(1.0f - z * z, 0.0f);
     return expf(beta * (sqrtf(t) - 1.0f));
+}
+
+// All W weights psi(l - fr), l = 0..W-1, by Horner evaluation of the
+// plan's per-tap polynomials in t = fr - (W/2 - 1/2).
+template <int W>
+__device__ __forceinline__ void es_weights(float fr, const EsPoly& P,
+                                           float* wt) {
+    constexpr int D = es_degree(W);
+    const float t = fr - (0.5f * W - 0.5f);
+#pragma unroll
+    for (int l = 0; l < W; ++l) wt[l] = P.c[D][l];
+#pragma unroll
+    for (int k = D - 1; k >= 0; --k)
+#pragma unroll
+        for (int l = 0; l < W; ++l) wt[l] = fmaf(wt[l], t, P.c[k][l]);
+}
+
+// Cyclic left rotation by one (compile-time indices only).
+template <int W, typename T>
+__device__ __forceinline__ void rotate(T* a) {
+    const T first = a[0];
+#pragma unroll
+    for (int l = 0; l < W - 1; ++l) a[l] = a[l + 1];
+    a[W - 1] = first;
 }
 
 __device__ __forceinline__ float2 cmul(float2 a, float2 b) {
@@ -92,13 +124,140 @@ __device__ __forceinline__ bool point_weights(const CellPtrs& cells, int64_t j,
         int2 cl = __ldg(cells.d[d] + j);
         l0[d] = cl.x - o[d];
         ok &= (unsigned)l0[d] < (unsigned)tg.m[d];
-        float fr = __int_as_float(cl.y);
-#pragma unroll
-        for (int l = 0; l < W; ++l)
-            wgt[d][l] = es_weight((float)l - fr, tg.c2w, tg.beta);
+        es_weights<W>(__int_as_float(cl.y), tg.poly, wgt[d]);
     }
     return ok;
 }
+
+// --------------------------------------------------------------------
+// shared-tile accumulate / gather of one point (cv already weighted by the
+// point's phase).  tv: interleaved complex tile as floats.
+template <int DIM, int W>
+__device__ __forceinline__ void tile_add(float* tv, const TileGeom& tg,
+                                         const int (&l0)[DIM],
+                                         float (&wgt)[DIM][W], float2 cv) {
+    if constexpr (DIM == 1) {
+#pragma unroll
+        for (int a = 0; a < W; ++a) {
+            const int q = 2 * (l0[0] + a);
+            atomicAdd(tv + q, cv.x * wgt[0][a]);
+            atomicAdd(tv + q + 1, cv.y * wgt[0][a]);
+        }
+    } else if constexpr (DIM == 2) {
+#pragma unroll
+        for (int a = 0; a < W; ++a) {
+            const float2 ca = make_float2(cv.x * wgt[0][a], cv.y * wgt[0][a]);
+            const int row = (l0[0] + a) * tg.T[1] + l0[1];
+#pragma unroll
+            for (int b = 0; b < W; ++b) {
+                const int q = 2 * (row + b);
+                atomicAdd(tv + q, ca.x * wgt[1][b]);
+                atomicAdd(tv + q + 1, ca.y * wgt[1][b]);
+            }
+        }
+    } else {
+        const int plane = tg.T[1] * tg.T[2];
+        int base = l0[0] * plane + l0[1] * tg.T[2] + l0[2];
+#pragma unroll 1
+        for (int a = 0; a < W; ++a, base += plane) {
+            const float wa = wgt[0][0];
+            const float2 ca = make_float2(cv.x * wa, cv.y * wa);
+#pragma unroll
+            for (int b = 0; b < W; ++b) {
+                const float2 cab = make_float2(ca.x * wgt[1][b], ca.y * wgt[1][b]);
+                const int q0 = 2 * (base + b * tg.T[2]);
+#pragma unroll
+                for (int k = 0; k < W; ++k) {
+                    atomicAdd(tv + q0 + 2 * k, cab.x * wgt[2][k]);
+                    atomicAdd(tv + q0 + 2 * k + 1, cab.y * wgt[2][k]);
+                }
+            }
+            rotate<W>(wgt[0]);
+        }
+    }
+}
+
+template <int DIM, int W>
+__device__ __forceinline__ float2 tile_gather(const float2* tv,
+                                              const TileGeom& tg,
+                                              const int (&l0)[DIM],
+                                              float (&wgt)[DIM][W]) {
+    float2 acc = make_float2(0.0f, 0.0f);
+    if constexpr (DIM == 1) {
+#pragma unroll
+        for (int a = 0; a < W; ++a) {
+            const float2 g = tv[l0[0] + a];
+            acc.x = fmaf(g.x, wgt[0][a], acc.x);
+            acc.y = fmaf(g.y, wgt[0][a], acc.y);
+        }
+    } else if constexpr (DIM == 2) {
+#pragma unroll
+        for (int a = 0; a < W; ++a) {
+            const int row = (l0[0] + a) * tg.T[1] + l0[1];
+            float2 s = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int b = 0; b < W; ++b) {
+                const float2 g = tv[row + b];
+                s.x = fmaf(g.x, wgt[1][b], s.x);
+                s.y = fmaf(g.y, wgt[1][b], s.y);
+            }
+            acc.x = fmaf(s.x, wgt[0][a], acc.x);
+            acc.y = fmaf(s.y, wgt[0][a], acc.y);
+        }
+    } else {
+        const int plane = tg.T[1] * tg.T[2];
+        int base = l0[0] * plane + l0[1] * tg.T[2] + l0[2];
+#pragma unroll 1
+        for (int a = 0; a < W; ++a, base += plane) {
+            float2 sa = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int b = 0; b < W; ++b) {
+                const float2* row = tv + base + b * tg.T[2];
+                float2 s = make_float2(0.0f, 0.0f);
+#pragma unroll
+                for (int k = 0; k < W; ++k) {
+                    const float2 g = row[k];
+                    s.x = fmaf(g.x, wgt[2][k], s.x);
+                    s.y = fmaf(g.y, wgt[2][k], s.y);
+                }
+                sa.x = fmaf(s.x, wgt[1][b], sa.x);
+                sa.y = fmaf(s.y, wgt[1][b], sa.y);
+            }
+            acc.x = fmaf(sa.x, wgt[0][0], acc.x);
+            acc.y = fmaf(sa.y, wgt[0][0], acc.y);
+            rotate<W>(wgt[0]);
+        }
+    }
+    return acc;
+}
+
+// --------------------------------------------------------------------
+// Dynamic subproblem scheduler of the persistent tiled kernels.  sched[0]
+// hands out subproblem indices; sched[1] counts CTAs that found no more
+// work; the last such CTA resets both, so the next launch on the stream
+// starts from zero without a memset.
+__device__ __forceinline__ int next_subproblem(int* sched, int* s_sub) {
+    if (threadIdx.x == 0) *s_sub = atomicAdd(&sched[0], 1);
+    __syncthreads();
+    return *s_sub;
+}
+
+__device__ __forceinline__ void scheduler_done(int* sched) {
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(&sched[1], 1) == (int)gridDim.x - 1) {
+            atomicExch(&sched[0], 0);
+            atomicExch(&sched[1], 0);
+        }
+    }
+}
+
+// Points of a subproblem are processed in batches of U per thread: the
+// loads of a whole batch (cells, permutation, phase: streamed once, so
+// cache-streaming hints) are issued before any of its math, keeping U
+// independent DRAM requests in flight per thread.
+template <int DIM>
+__host__ __device__ constexpr int batch_u() { return DIM == 3 ? 2 : 4; }
 
 // --------------------------------------------------------------------
 // tiled spread: grid[v] += sum_j c[v][perm j] * phase_j * psi-tensor
@@ -107,76 +266,68 @@ __global__ void __launch_bounds__(256)
 k_spread_tiled(const float2* __restrict__ c, int64_t cstride, int nvg,
                const uint32_t* __restrict__ perm, CellPtrs cells,
                const float2* __restrict__ phase, const int4* __restrict__ subs,
-               float2* __restrict__ grid, TileGeom tg) {
+               int nsub, int* __restrict__ sched, float2* __restrict__ grid,
+               TileGeom tg) {
     extern __shared__ float2 tile[];
-    const int4 sb = subs[blockIdx.x];
-    const int start = sb.x, cnt = sb.y;
-    int o[3] = {0, 0, 0};
-    bin_origin<DIM>(sb.z, tg, o);
+    __shared__ int s_sub;
+    constexpr int U = batch_u<DIM>();
     const int T = tg.tcells;
-    for (int q = threadIdx.x; q < nvg * T; q += blockDim.x)
-        tile[q] = make_float2(0.0f, 0.0f);
-    __syncthreads();
-    for (int t = threadIdx.x; t < cnt; t += blockDim.x) {
-        const int64_t j = start + t;
-        const int64_t src = perm ? (int64_t)__ldg(perm + j) : j;
-        float wgt[DIM][W];
-        int l0[DIM];
-        if (!point_weights<DIM, W>(cells, j, o, tg, wgt, l0)) continue;
-        const float2 ph = phase ? __ldg(phase + j) : make_float2(1.0f, 0.0f);
-        for (int v = 0; v < nvg; ++v) {
-            float2 cv = __ldg(c + v * cstride + src);
-            if (phase) cv = cmul(cv, ph);
-            float* tv = reinterpret_cast<float*>(tile + v * T);
-            if (DIM == 1) {
+    for (;;) {
+        const int sub = next_subproblem(sched, &s_sub);
+        if (sub >= nsub) break;
+        const int4 sb = subs[sub];
+        const int start = sb.x, cnt = sb.y;
+        int o[3] = {0, 0, 0};
+        bin_origin<DIM>(sb.z, tg, o);
+        for (int q = threadIdx.x; q < nvg * T; q += blockDim.x)
+            tile[q] = make_float2(0.0f, 0.0f);
+        __syncthreads();
+        for (int base = 0; base < cnt; base += U * blockDim.x) {
+            int2 cl[U][DIM];
+            int64_t src[U];
+            float2 ph[U];
 #pragma unroll
-                for (int a = 0; a < W; ++a) {
-                    const int q = 2 * (l0[0] + a);
-                    atomicAdd(tv + q, cv.x * wgt[0][a]);
-                    atomicAdd(tv + q + 1, cv.y * wgt[0][a]);
+            for (int u = 0; u < U; ++u) {
+                const int t = base + u * blockDim.x + threadIdx.x;
+                const int64_t j = start + min(t, cnt - 1);
+#pragma unroll
+                for (int d = 0; d < DIM; ++d) cl[u][d] = __ldcs(cells.d[d] + j);
+                src[u] = perm ? (int64_t)__ldcs(perm + j) : j;
+                ph[u] = phase ? __ldcs(phase + j) : make_float2(1.0f, 0.0f);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                if (base + u * (int)blockDim.x + (int)threadIdx.x >= cnt) break;
+                float wgt[DIM][W];
+                int l0[DIM];
+                bool ok = true;
+#pragma unroll
+                for (int d = 0; d < DIM; ++d) {
+                    l0[d] = cl[u][d].x - o[d];
+                    ok &= (unsigned)l0[d] < (unsigned)tg.m[d];
+                    es_weights<W>(__int_as_float(cl[u][d].y), tg.poly, wgt[d]);
                 }
-            } else if (DIM == 2) {
-#pragma unroll
-                for (int a = 0; a < W; ++a) {
-                    const float2 ca = make_float2(cv.x * wgt[0][a], cv.y * wgt[0][a]);
-                    const int row = (l0[0] + a) * tg.T[1] + l0[DIM > 1 ? 1 : 0];
-#pragma unroll
-                    for (int b = 0; b < W; ++b) {
-                        const int q = 2 * (row + b);
-                        atomicAdd(tv + q, ca.x * wgt[DIM > 1 ? 1 : 0][b]);
-                        atomicAdd(tv + q + 1, ca.y * wgt[DIM > 1 ? 1 : 0][b]);
-                    }
-                }
-            } else {
-#pragma unroll 1
-                for (int a = 0; a < W; ++a) {
-#pragma unroll
-                    for (int b = 0; b < W; ++b) {
-                        const float wab = wgt[0][a] * wgt[DIM > 1 ? 1 : 0][b];
-                        const float2 cab = make_float2(cv.x * wab, cv.y * wab);
-                        const int base =
-                            ((l0[0] + a) * tg.T[1] + l0[DIM > 1 ? 1 : 0] + b) *
-                                tg.T[DIM > 2 ? 2 : 0] + l0[DIM > 2 ? 2 : 0];
-#pragma unroll
-                        for (int k = 0; k < W; ++k) {
-                            const int q = 2 * (base + k);
-                            atomicAdd(tv + q, cab.x * wgt[DIM > 2 ? 2 : 0][k]);
-                            atomicAdd(tv + q + 1, cab.y * wgt[DIM > 2 ? 2 : 0][k]);
-                        }
-                    }
+                if (!ok) continue;
+                for (int v = 0; v < nvg; ++v) {
+                    float2 cv = __ldg(c + v * cstride + src[u]);
+                    if (phase) cv = cmul(cv, ph[u]);
+                    tile_add<DIM, W>(reinterpret_cast<float*>(tile + v * T), tg,
+                                     l0, wgt, cv);
                 }
             }
         }
-    }
-    __syncthreads();
-    for (int q = threadIdx.x; q < T; q += blockDim.x) {
-        const int64_t g = tile_to_global<DIM>(q, o, tg);
-        for (int v = 0; v < nvg; ++v) {
-            const float2 val = tile[v * T + q];
-            if (val.x != 0.0f || val.y != 0.0f)
-                atomicAdd(grid + v * tg.ncells + g, val);
+        __syncthreads();
+        for (int q = threadIdx.x; q < T; q += blockDim.x) {
+            const int64_t g = tile_to_global<DIM>(q, o, tg);
+            for (int v = 0; v < nvg; ++v) {
+                const float2 val = tile[v * T + q];
+                if (val.x != 0.0f || val.y != 0.0f)
+                    atomicAdd(grid + v * tg.ncells + g, val);
+            }
         }
+        __syncthreads();
     }
+    scheduler_done(sched);
 }
 
 // --------------------------------------------------------------------
@@ -186,77 +337,63 @@ __global__ void __launch_bounds__(256)
 k_interp_tiled(const float2* __restrict__ grid, int nvg,
                const uint32_t* __restrict__ perm, CellPtrs cells,
                const float2* __restrict__ phase, const int4* __restrict__ subs,
-               float2* __restrict__ out, int64_t ostride, TileGeom tg) {
+               int nsub, int* __restrict__ sched, float2* __restrict__ out,
+               int64_t ostride, TileGeom tg) {
     extern __shared__ float2 tile[];
-    const int4 sb = subs[blockIdx.x];
-    const int start = sb.x, cnt = sb.y;
-    int o[3] = {0, 0, 0};
-    bin_origin<DIM>(sb.z, tg, o);
+    __shared__ int s_sub;
+    constexpr int U = batch_u<DIM>();
     const int T = tg.tcells;
-    for (int q = threadIdx.x; q < T; q += blockDim.x) {
-        const int64_t g = tile_to_global<DIM>(q, o, tg);
-        for (int v = 0; v < nvg; ++v)
-            tile[v * T + q] = __ldg(grid + v * tg.ncells + g);
-    }
-    __syncthreads();
-    for (int t = threadIdx.x; t < cnt; t += blockDim.x) {
-        const int64_t j = start + t;
-        const int64_t dst = perm ? (int64_t)__ldg(perm + j) : j;
-        float wgt[DIM][W];
-        int l0[DIM];
-        const bool ok = point_weights<DIM, W>(cells, j, o, tg, wgt, l0);
-        const float2 ph = phase ? __ldg(phase + j) : make_float2(1.0f, 0.0f);
-        for (int v = 0; v < nvg; ++v) {
-            const float2* tv = tile + v * T;
-            float2 acc = make_float2(0.0f, 0.0f);
-            if (ok) {
-                if (DIM == 1) {
-#pragma unroll
-                    for (int a = 0; a < W; ++a) {
-                        const float2 g = tv[l0[0] + a];
-                        acc.x = fmaf(g.x, wgt[0][a], acc.x);
-                        acc.y = fmaf(g.y, wgt[0][a], acc.y);
-                    }
-                } else if (DIM == 2) {
-#pragma unroll
-                    for (int a = 0; a < W; ++a) {
-                        const int row = (l0[0] + a) * tg.T[1] + l0[DIM > 1 ? 1 : 0];
-                        float2 s = make_float2(0.0f, 0.0f);
-#pragma unroll
-                        for (int b = 0; b < W; ++b) {
-                            const float2 g = tv[row + b];
-                            s.x = fmaf(g.x, wgt[DIM > 1 ? 1 : 0][b], s.x);
-                            s.y = fmaf(g.y, wgt[DIM > 1 ? 1 : 0][b], s.y);
-                        }
-                        acc.x = fmaf(s.x, wgt[0][a], acc.x);
-                        acc.y = fmaf(s.y, wgt[0][a], acc.y);
-                    }
-                } else {
-#pragma unroll 1
-                    for (int a = 0; a < W; ++a) {
-#pragma unroll
-                        for (int b = 0; b < W; ++b) {
-                            const float wab = wgt[0][a] * wgt[DIM > 1 ? 1 : 0][b];
-                            const int base =
-                                ((l0[0] + a) * tg.T[1] + l0[DIM > 1 ? 1 : 0] + b) *
-                                    tg.T[DIM > 2 ? 2 : 0] + l0[DIM > 2 ? 2 : 0];
-                            float2 s = make_float2(0.0f, 0.0f);
-#pragma unroll
-                            for (int k = 0; k < W; ++k) {
-                                const float2 g = tv[base + k];
-                                s.x = fmaf(g.x, wgt[DIM > 2 ? 2 : 0][k], s.x);
-                                s.y = fmaf(g.y, wgt[DIM > 2 ? 2 : 0][k], s.y);
-                            }
-                            acc.x = fmaf(s.x, wab, acc.x);
-                            acc.y = fmaf(s.y, wab, acc.y);
-                        }
-                    }
-                }
-                if (phase) acc = cmul(acc, ph);
-            }
-            out[v * ostride + dst] = acc;
+    for (;;) {
+        const int sub = next_subproblem(sched, &s_sub);
+        if (sub >= nsub) break;
+        const int4 sb = subs[sub];
+        const int start = sb.x, cnt = sb.y;
+        int o[3] = {0, 0, 0};
+        bin_origin<DIM>(sb.z, tg, o);
+        for (int q = threadIdx.x; q < T; q += blockDim.x) {
+            const int64_t g = tile_to_global<DIM>(q, o, tg);
+            for (int v = 0; v < nvg; ++v)
+                tile[v * T + q] = __ldg(grid + v * tg.ncells + g);
         }
+        __syncthreads();
+        for (int base = 0; base < cnt; base += U * blockDim.x) {
+            int2 cl[U][DIM];
+            int64_t dst[U];
+            float2 ph[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int t = base + u * blockDim.x + threadIdx.x;
+                const int64_t j = start + min(t, cnt - 1);
+#pragma unroll
+                for (int d = 0; d < DIM; ++d) cl[u][d] = __ldcs(cells.d[d] + j);
+                dst[u] = perm ? (int64_t)__ldcs(perm + j) : j;
+                ph[u] = phase ? __ldcs(phase + j) : make_float2(1.0f, 0.0f);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                if (base + u * (int)blockDim.x + (int)threadIdx.x >= cnt) break;
+                float wgt[DIM][W];
+                int l0[DIM];
+                bool ok = true;
+#pragma unroll
+                for (int d = 0; d < DIM; ++d) {
+                    l0[d] = cl[u][d].x - o[d];
+                    ok &= (unsigned)l0[d] < (unsigned)tg.m[d];
+                    es_weights<W>(__int_as_float(cl[u][d].y), tg.poly, wgt[d]);
+                }
+                for (int v = 0; v < nvg; ++v) {
+                    float2 acc = make_float2(0.0f, 0.0f);
+                    if (ok) {
+                        acc = tile_gather<DIM, W>(tile + v * T, tg, l0, wgt);
+                        if (phase) acc = cmul(acc, ph[u]);
+                    }
+                    out[v * ostride + dst[u]] = acc;
+                }
+            }
+        }
+        __syncthreads();
     }
+    scheduler_done(sched);
 }
 
 // --------------------------------------------------------------------
@@ -269,13 +406,104 @@ __device__ __forceinline__ void global_taps(const CellPtrs& cells, int64_t j,
 #pragma unroll
     for (int d = 0; d < DIM; ++d) {
         int2 cl = __ldg(cells.d[d] + j);
-        float fr = __int_as_float(cl.y);
+        es_weights<W>(__int_as_float(cl.y), tg.poly, wgt[d]);
 #pragma unroll
-        for (int l = 0; l < W; ++l) {
-            wgt[d][l] = es_weight((float)l - fr, tg.c2w, tg.beta);
-            idx[d][l] = wrap1(cl.x + l, tg.n[d]);
+        for (int l = 0; l < W; ++l) idx[d][l] = wrap1(cl.x + l, tg.n[d]);
+    }
+}
+
+// grid[...] += cv * psi-tensor with global float2 atomics
+template <int DIM, int W>
+__device__ __forceinline__ void global_add(float2* gv, const TileGeom& tg,
+                                           float (&wgt)[DIM][W],
+                                           int (&idx)[DIM][W], float2 cv) {
+    if constexpr (DIM == 1) {
+#pragma unroll
+        for (int a = 0; a < W; ++a)
+            atomicAdd(gv + idx[0][a], make_float2(cv.x * wgt[0][a], cv.y * wgt[0][a]));
+    } else if constexpr (DIM == 2) {
+#pragma unroll
+        for (int a = 0; a < W; ++a) {
+            const int64_t row = (int64_t)idx[0][a] * tg.n[1];
+#pragma unroll
+            for (int b = 0; b < W; ++b) {
+                const float wab = wgt[0][a] * wgt[1][b];
+                atomicAdd(gv + row + idx[1][b], make_float2(cv.x * wab, cv.y * wab));
+            }
+        }
+    } else {
+#pragma unroll 1
+        for (int a = 0; a < W; ++a) {
+            const int64_t plane = (int64_t)idx[0][0] * tg.n[1];
+            const float wa = wgt[0][0];
+#pragma unroll
+            for (int b = 0; b < W; ++b) {
+                const float wab = wa * wgt[1][b];
+                const int64_t base = (plane + idx[1][b]) * tg.n[2];
+#pragma unroll
+                for (int k = 0; k < W; ++k) {
+                    const float wk = wab * wgt[2][k];
+                    atomicAdd(gv + base + idx[2][k], make_float2(cv.x * wk, cv.y * wk));
+                }
+            }
+            rotate<W>(wgt[0]);
+            rotate<W>(idx[0]);
         }
     }
+}
+
+template <int DIM, int W>
+__device__ __forceinline__ float2 global_gather(const float2* gv,
+                                                const TileGeom& tg,
+                                                float (&wgt)[DIM][W],
+                                                int (&idx)[DIM][W]) {
+    float2 acc = make_float2(0.0f, 0.0f);
+    if constexpr (DIM == 1) {
+#pragma unroll
+        for (int a = 0; a < W; ++a) {
+            const float2 g = __ldg(gv + idx[0][a]);
+            acc.x = fmaf(g.x, wgt[0][a], acc.x);
+            acc.y = fmaf(g.y, wgt[0][a], acc.y);
+        }
+    } else if constexpr (DIM == 2) {
+#pragma unroll
+        for (int a = 0; a < W; ++a) {
+            const int64_t row = (int64_t)idx[0][a] * tg.n[1];
+            float2 s = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int b = 0; b < W; ++b) {
+                const float2 g = __ldg(gv + row + idx[1][b]);
+                s.x = fmaf(g.x, wgt[1][b], s.x);
+                s.y = fmaf(g.y, wgt[1][b], s.y);
+            }
+            acc.x = fmaf(s.x, wgt[0][a], acc.x);
+            acc.y = fmaf(s.y, wgt[0][a], acc.y);
+        }
+    } else {
+#pragma unroll 1
+        for (int a = 0; a < W; ++a) {
+            const int64_t plane = (int64_t)idx[0][0] * tg.n[1];
+            float2 sa = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int b = 0; b < W; ++b) {
+                const float2* row = gv + (plane + idx[1][b]) * tg.n[2];
+                float2 s = make_float2(0.0f, 0.0f);
+#pragma unroll
+                for (int k = 0; k < W; ++k) {
+                    const float2 g = __ldg(row + idx[2][k]);
+                    s.x = fmaf(g.x, wgt[2][k], s.x);
+                    s.y = fmaf(g.y, wgt[2][k], s.y);
+                }
+                sa.x = fmaf(s.x, wgt[1][b], sa.x);
+                sa.y = fmaf(s.y, wgt[1][b], sa.y);
+            }
+            acc.x = fmaf(sa.x, wgt[0][0], acc.x);
+            acc.y = fmaf(sa.y, wgt[0][0], acc.y);
+            rotate<W>(wgt[0]);
+            rotate<W>(idx[0]);
+        }
+    }
+    return acc;
 }
 
 template <int DIM, int W>
@@ -294,41 +522,7 @@ k_spread_global(const float2* __restrict__ c, int64_t cstride, int nvec,
     for (int v = 0; v < nvec; ++v) {
         float2 cv = __ldg(c + v * cstride + src);
         if (phase) cv = cmul(cv, ph);
-        float2* gv = grid + v * tg.ncells;
-        if (DIM == 1) {
-#pragma unroll
-            for (int a = 0; a < W; ++a)
-                atomicAdd(gv + idx[0][a],
-                          make_float2(cv.x * wgt[0][a], cv.y * wgt[0][a]));
-        } else if (DIM == 2) {
-#pragma unroll
-            for (int a = 0; a < W; ++a) {
-                const int64_t row = (int64_t)idx[0][a] * tg.n[1];
-#pragma unroll
-                for (int b = 0; b < W; ++b) {
-                    const float wab = wgt[0][a] * wgt[DIM > 1 ? 1 : 0][b];
-                    atomicAdd(gv + row + idx[DIM > 1 ? 1 : 0][b],
-                              make_float2(cv.x * wab, cv.y * wab));
-                }
-            }
-        } else {
-#pragma unroll 1
-            for (int a = 0; a < W; ++a) {
-#pragma unroll
-                for (int b = 0; b < W; ++b) {
-                    const float wab = wgt[0][a] * wgt[DIM > 1 ? 1 : 0][b];
-                    const int64_t base =
-                        ((int64_t)idx[0][a] * tg.n[1] + idx[DIM > 1 ? 1 : 0][b]) *
-                        tg.n[DIM > 2 ? 2 : 0];
-#pragma unroll
-                    for (int k = 0; k < W; ++k) {
-                        const float wk = wab * wgt[DIM > 2 ? 2 : 0][k];
-                        atomicAdd(gv + base + idx[DIM > 2 ? 2 : 0][k],
-                                  make_float2(cv.x * wk, cv.y * wk));
-                    }
-                }
-            }
-        }
+        global_add<DIM, W>(grid + v * tg.ncells, tg, wgt, idx, cv);
     }
 }
 
@@ -346,50 +540,7 @@ k_interp_global(const float2* __restrict__ grid, int nvec,
     global_taps<DIM, W>(cells, j, tg, wgt, idx);
     const float2 ph = phase ? __ldg(phase + j) : make_float2(1.0f, 0.0f);
     for (int v = 0; v < nvec; ++v) {
-        const float2* gv = grid + v * tg.ncells;
-        float2 acc = make_float2(0.0f, 0.0f);
-        if (DIM == 1) {
-#pragma unroll
-            for (int a = 0; a < W; ++a) {
-                const float2 g = __ldg(gv + idx[0][a]);
-                acc.x = fmaf(g.x, wgt[0][a], acc.x);
-                acc.y = fmaf(g.y, wgt[0][a], acc.y);
-            }
-        } else if (DIM == 2) {
-#pragma unroll
-            for (int a = 0; a < W; ++a) {
-                const int64_t row = (int64_t)idx[0][a] * tg.n[1];
-                float2 s = make_float2(0.0f, 0.0f);
-#pragma unroll
-                for (int b = 0; b < W; ++b) {
-                    const float2 g = __ldg(gv + row + idx[DIM > 1 ? 1 : 0][b]);
-                    s.x = fmaf(g.x, wgt[DIM > 1 ? 1 : 0][b], s.x);
-                    s.y = fmaf(g.y, wgt[DIM > 1 ? 1 : 0][b], s.y);
-                }
-                acc.x = fmaf(s.x, wgt[0][a], acc.x);
-                acc.y = fmaf(s.y, wgt[0][a], acc.y);
-            }
-        } else {
-#pragma unroll 1
-            for (int a = 0; a < W; ++a) {
-#pragma unroll
-                for (int b = 0; b < W; ++b) {
-                    const float wab = wgt[0][a] * wgt[DIM > 1 ? 1 : 0][b];
-                    const int64_t base =
-                        ((int64_t)idx[0][a] * tg.n[1] + idx[DIM > 1 ? 1 : 0][b]) *
-                        tg.n[DIM > 2 ? 2 : 0];
-                    float2 s = make_float2(0.0f, 0.0f);
-#pragma unroll
-                    for (int k = 0; k < W; ++k) {
-                        const float2 g = __ldg(gv + base + idx[DIM > 2 ? 2 : 0][k]);
-                        s.x = fmaf(g.x, wgt[DIM > 2 ? 2 : 0][k], s.x);
-                        s.y = fmaf(g.y, wgt[DIM > 2 ? 2 : 0][k], s.y);
-                    }
-                    acc.x = fmaf(s.x, wab, acc.x);
-                    acc.y = fmaf(s.y, wab, acc.y);
-                }
-            }
-        }
+        float2 acc = global_gather<DIM, W>(grid + v * tg.ncells, tg, wgt, idx);
         if (phase) acc = cmul(acc, ph);
         out[v * ostride + dst] = acc;
     }

@@ -30,8 +30,9 @@ EXPI_MAX_PHASE = float(2 ** 24 * 2.0 * PI)
 def _as_f64_array(v, device):
     if isinstance(v, torch.Tensor):
         return v.detach().to(device=device, dtype=torch.float64).contiguous()
-    a = np.asarray(v, dtype=np.float64)
-    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+    # np.array (not ascontiguousarray, which promotes 0-d input to 1-d)
+    a = np.array(v, dtype=np.float64, copy=True, order="C")
+    return torch.from_numpy(a).to(device)
 
 
 def expi(phases, isign=1, return_np=False):

@@ -298,6 +298,72 @@ def nufft_t3(x, c, s, eps=1e-5, isign=+1, upsampfac=1.25, geom=None):
     return interp(V, g.t_i1, g.t_fr, g.w, g.beta) * g.post
 
 
+def _kernel_1d_f32(fr, w, beta):
+    """ref_t3.py:140-154 with dtype float32: the fp32 ES weights."""
+    f32 = np.float32
+    l = np.arange(w, dtype=f32)
+    d = l[None, :] - np.asarray(fr, dtype=f32)[:, None]
+    z2 = (f32(2.0 / w) * d) ** 2
+    out = np.exp(f32(beta) * (np.sqrt(np.maximum(f32(1.0) - z2, f32(0.0)))
+                              - f32(1.0)))
+    out[z2 > 1.0] = 0.0
+    return out
+
+
+def nufft_t3_fp32(x, c, s, eps=1e-5, isign=+1, upsampfac=1.25, chunk=2048):
+    """The reference's fp32 type-3 pipeline with crit64 geometry: fp64
+    coordinates and phases, fp32 spread / FFT / interp / deconvolution
+    (ref_t3.py:156-221 executed with Flags(coords64=True, phases64=True,
+    spread64=False, fft64=False, interp64=False, deconv64=False)).  Its
+    error against the exact sum is the accuracy floor an fp32 device
+    pipeline of this algorithm has on the given inputs."""
+    g = T3Geometry(x, s, eps, isign, upsampfac)
+    dim, w = g.dim, g.w
+    cp = (np.asarray(c, dtype=np.complex128) * g.prephase).astype(np.complex64)
+    fr = [v.astype(np.float32) for v in g.fr]
+    B = np.zeros(int(np.prod(g.nf)), dtype=np.complex64)
+    P = cp.size
+    for a0 in range(0, P, chunk):
+        sl = slice(a0, min(a0 + chunk, P))
+        m = sl.stop - sl.start
+        vals = cp[sl].reshape((m,) + (1,) * dim)
+        flat = np.zeros((m,) + (1,) * dim, dtype=np.int64)
+        for d in range(dim):
+            shp = (m,) + (1,) * d + (w,) + (1,) * (dim - d - 1)
+            vals = vals * _kernel_1d_f32(fr[d][sl], w, g.beta).reshape(shp)
+            idx = (g.i1[d][sl, None] + np.arange(w)) % g.nf[d]
+            flat = flat * g.nf[d] + idx.reshape(shp)
+        np.add.at(B, flat.ravel(), vals.ravel())
+    B = B.reshape(g.nf)
+    dec = np.ones(g.nf, dtype=np.float32)
+    for d in range(dim):
+        dec = dec * g.mode_dec[d].astype(np.float32).reshape(
+            (1,) * d + (-1,) + (1,) * (dim - d - 1))
+    H = np.zeros(g.n_up, dtype=np.complex64)
+    H[np.ix_(*[np.mod(np.arange(-g.nf[d] // 2, g.nf[d] // 2), g.n_up[d])
+               for d in range(dim)])] = (B * dec).astype(np.complex64)
+    if g.isign > 0:
+        V = np.fft.ifftn(H) * int(np.prod(g.n_up))
+    else:
+        V = np.fft.fftn(H)
+    V = V.astype(np.complex64).ravel()
+    t_fr = [v.astype(np.float32) for v in g.t_fr]
+    M = g.t_i1[0].size
+    out = np.zeros(M, dtype=np.complex64)
+    for a0 in range(0, M, chunk):
+        sl = slice(a0, min(a0 + chunk, M))
+        m = sl.stop - sl.start
+        wgt = np.ones((m,) + (1,) * dim, dtype=np.float32)
+        flat = np.zeros((m,) + (1,) * dim, dtype=np.int64)
+        for d in range(dim):
+            shp = (m,) + (1,) * d + (w,) + (1,) * (dim - d - 1)
+            wgt = wgt * _kernel_1d_f32(t_fr[d][sl], w, g.beta).reshape(shp)
+            idx = (g.t_i1[d][sl, None] + np.arange(w)) % g.n_up[d]
+            flat = flat * g.n_up[d] + idx.reshape(shp)
+        out[sl] = (V[flat] * wgt).sum(axis=tuple(range(1, dim + 1)))
+    return out * g.post.astype(np.complex64)
+
+
 # --------------------------------------------------------------------------
 # exact direct sums (harness/gen.py:93-119) and error metric (gen.py:122-125)
 

@@ -94,10 +94,18 @@ def make_t3(ref_t3, gen):
                                 flags=ref_t3.FULL64)
         f = plan.execute(c)
         fd = gen.direct_sum(x, c, s, isign=cs["isign"])
+        # the reference's fp32 pipeline with crit64 geometry (fp64 coords
+        # and phases, fp32 spread/FFT/interp/deconvolution): the accuracy
+        # floor its GPU path is designed to (ref_t3.py:29-48)
+        crit32 = ref_t3.Flags(coords64=True, phases64=True, spread64=False,
+                              fft64=False, interp64=False, deconv64=False)
+        f32 = ref_t3.RefT3Plan(x, s, eps=cs["eps"], isign=cs["isign"],
+                               flags=crit32).execute(c)
         pre = f"c{i}_"
         out.update({pre + "x": np.stack(x), pre + "s": np.stack(s),
                     pre + "c": c, pre + "eps": cs["eps"],
                     pre + "isign": cs["isign"], pre + "out": f,
+                    pre + "out32": f32,
                     pre + "direct": fd, pre + "nf": np.array(plan.nf),
                     pre + "n_up": np.array(plan.n_up), pre + "w": plan.w,
                     pre + "beta": plan.beta, pre + "C": np.array(plan.C),

@@ -133,3 +133,14 @@ def test_oracle_cells_fold_matches_formula():
     xi = np.mod(x, 2 * np.pi) / (2 * np.pi / 64)
     np.testing.assert_array_equal(i1, np.ceil(xi - 3.5).astype(np.int32))
     assert np.all(fr64 > 2.5 - 1e-12) and np.all(fr64 <= 3.5)
+
+
+@pytest.mark.parametrize("case", [0, 1, 2])
+def test_type3_fp32_pipeline_matches_ref_t3(golden, case):
+    """oracle.port.nufft_t3_fp32 reproduces the reference's fp32 type-3
+    pipeline (RefT3Plan with crit64 geometry, fp32 stages) bit for bit."""
+    g = golden("t3_ref")
+    p = f"c{case}_"
+    f = port.nufft_t3_fp32(list(g[p + "x"]), g[p + "c"], list(g[p + "s"]),
+                           eps=float(g[p + "eps"]), isign=int(g[p + "isign"]))
+    np.testing.assert_array_equal(f, g[p + "out32"])
