@@ -74,6 +74,11 @@ typedef struct nufft_opts {
     int    profile;        /* 1: record CUDA events around every stage             */
     int    has_source_extent;  /* type 3: size from source_extent, not from x     */
     double source_extent[6];   /* type 3: (lo, hi) per dimension                  */
+    int    kerevalmeth;    /* ES kernel evaluation (finufft spread_kerevalmeth): */
+                           /* 1 per-tap polynomials (default), 0 exp/sqrt      */
+    int    fft_prec;       /* fine-grid FFT precision: 0 auto (fp64 when the   */
+                           /* upsampling is < 1.5 and eps < 1e-4), 1 fp32,     */
+                           /* 2 fp64                                           */
 } nufft_opts;
 
 typedef struct nufft_plan_info {

@@ -39,6 +39,8 @@ class NufftOpts(ctypes.Structure):
         ("profile", ctypes.c_int),
         ("has_source_extent", ctypes.c_int),
         ("source_extent", ctypes.c_double * 6),
+        ("kerevalmeth", ctypes.c_int),
+        ("fft_prec", ctypes.c_int),
     ]
 
 

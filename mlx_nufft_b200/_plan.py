@@ -22,9 +22,12 @@ class NativePlan:
     def __init__(self, nufft_type, dim, n_modes, n_trans, eps, isign,
                  upsampfac=None, sigma_inner=None, prec="crit64",
                  method="auto", sort_points=True, max_batch=0, profile=False,
-                 source_extent=None):
+                 source_extent=None, kerevalmeth=1):
         self.device = require_cuda()
         opts = _lib.default_opts()
+        if kerevalmeth not in (0, 1):
+            raise ValueError("kerevalmeth must be 0 (exp/sqrt) or 1 (polynomial)")
+        opts.kerevalmeth = int(kerevalmeth)
         opts.upsampfac = float(upsampfac) if upsampfac else 0.0
         opts.sigma_inner = float(sigma_inner) if sigma_inner else 0.0
         if prec not in _lib.PREC:

@@ -49,8 +49,14 @@ __device__ __forceinline__ void split_row(int64_t row, const int* ext, int dim,
 
 // Type-1 crop: fk[v][m] = grid[v][r(m)] * prod_d dec_d[m_d], with
 // r_d = m_d - N_d/2 (+ n_d if negative).
+__device__ __forceinline__ float2 to_f2(float2 v) { return v; }
+__device__ __forceinline__ float2 to_f2(double2 v) {
+    return make_float2((float)v.x, (float)v.y);
+}
+
+template <typename G>
 __global__ void __launch_bounds__(256)
-k_crop(const float2* __restrict__ grid, float2* __restrict__ fk, DecPtrs dec,
+k_crop(const G* __restrict__ grid, float2* __restrict__ fk, DecPtrs dec,
        BoxGrid bg, int chunks_per_row) {
     const int dim = bg.dim;
     const int L = dim - 1;                    // innermost dim index
@@ -71,8 +77,17 @@ k_crop(const float2* __restrict__ grid, float2* __restrict__ fk, DecPtrs dec,
     int r = m_in - bg.N[L] / 2;
     if (r < 0) r += bg.n[L];
     const float dd = (L == 0) ? dec.d[0][m_in] : dout * dec.d[L][m_in];
-    const float2 g = grid[v * bg.ncells + rrow * bg.n[L] + r];
+    const float2 g = to_f2(grid[v * bg.ncells + rrow * bg.n[L] + r]);
     fk[v * bg.K + row * bg.N[L] + m_in] = make_float2(g.x * dd, g.y * dd);
+}
+
+__global__ void __launch_bounds__(256)
+k_widen(const float2* __restrict__ in, double2* __restrict__ out, int64_t n) {
+    const int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (j < n) {
+        const float2 v = in[j];
+        out[j] = make_double2(v.x, v.y);
+    }
 }
 
 // Pad: H[v][r] = f[v][m(r)] * prod dec if every dim is in band, else 0.
@@ -80,8 +95,17 @@ k_crop(const float2* __restrict__ grid, float2* __restrict__ fk, DecPtrs dec,
 // -N/2 <= q < N - N/2; m = q + N/2.
 // Each thread writes two consecutive fine cells with one 16-byte store
 // (fine-grid extents are even, so rows stay 16-byte aligned).
+__device__ __forceinline__ void store_pair(float2* p, float4 v) {
+    *reinterpret_cast<float4*>(p) = v;
+}
+__device__ __forceinline__ void store_pair(double2* p, float4 v) {
+    p[0] = make_double2(v.x, v.y);
+    p[1] = make_double2(v.z, v.w);
+}
+
+template <typename H_T>
 __global__ void __launch_bounds__(256)
-k_pad(const float2* __restrict__ f, float2* __restrict__ H, DecPtrs dec,
+k_pad(const float2* __restrict__ f, H_T* __restrict__ H, DecPtrs dec,
       BoxGrid bg, int chunks_per_row) {
     const int dim = bg.dim;
     const int L = dim - 1;
@@ -122,7 +146,7 @@ k_pad(const float2* __restrict__ f, float2* __restrict__ H, DecPtrs dec,
             }
         }
     }
-    *reinterpret_cast<float4*>(H + v * bg.ncells + row * bg.n[L] + r0) = out;
+    store_pair(H + v * bg.ncells + row * bg.n[L] + r0, out);
 }
 
 namespace {
@@ -152,8 +176,8 @@ DecPtrs make_dec(const float* const* dec) {
 }  // namespace
 
 void launch_crop(int dim, const int64_t* N, const int64_t* n,
-                 const float* const* dec, const float2* grid, float2* fk,
-                 int nvec, cudaStream_t st) {
+                 const float* const* dec, const void* grid, bool grid64,
+                 float2* fk, int nvec, cudaStream_t st) {
     const BoxGrid bg = make_boxgrid(dim, N, n);
     const int inner = bg.N[dim - 1];
     const int cpr = (inner + 255) / 256;
@@ -163,15 +187,19 @@ void launch_crop(int dim, const int64_t* N, const int64_t* n,
     for (int v0 = 0; v0 < nvec; v0 += 65535) {
         const int nv = std::min(65535, nvec - v0);
         dim3 g((unsigned)blocks, (unsigned)nv);
-        k_crop<<<g, 256, 0, st>>>(grid + v0 * bg.ncells, fk + v0 * bg.K,
-                                  make_dec(dec), bg, cpr);
+        if (grid64)
+            k_crop<<<g, 256, 0, st>>>((const double2*)grid + v0 * bg.ncells,
+                                      fk + v0 * bg.K, make_dec(dec), bg, cpr);
+        else
+            k_crop<<<g, 256, 0, st>>>((const float2*)grid + v0 * bg.ncells,
+                                      fk + v0 * bg.K, make_dec(dec), bg, cpr);
         NUFFT_LAUNCH("k_crop");
     }
 }
 
 void launch_pad(int dim, const int64_t* N, const int64_t* n,
-                const float* const* dec, const float2* f, float2* H, int nvec,
-                cudaStream_t st) {
+                const float* const* dec, const float2* f, void* H,
+                bool grid64, int nvec, cudaStream_t st) {
     const BoxGrid bg = make_boxgrid(dim, N, n);
     const int inner = bg.n[dim - 1];
     if (inner % 2) fail(-1, "fine-grid extents must be even");
@@ -182,10 +210,20 @@ void launch_pad(int dim, const int64_t* N, const int64_t* n,
     for (int v0 = 0; v0 < nvec; v0 += 65535) {
         const int nv = std::min(65535, nvec - v0);
         dim3 g((unsigned)blocks, (unsigned)nv);
-        k_pad<<<g, 256, 0, st>>>(f + v0 * bg.K, H + v0 * bg.ncells,
-                                 make_dec(dec), bg, cpr);
+        if (grid64)
+            k_pad<<<g, 256, 0, st>>>(f + v0 * bg.K, (double2*)H + v0 * bg.ncells,
+                                     make_dec(dec), bg, cpr);
+        else
+            k_pad<<<g, 256, 0, st>>>(f + v0 * bg.K, (float2*)H + v0 * bg.ncells,
+                                     make_dec(dec), bg, cpr);
         NUFFT_LAUNCH("k_pad");
     }
+}
+
+void launch_widen(const float2* in, double2* out, int64_t n, cudaStream_t st) {
+    if (n <= 0) return;
+    k_widen<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(in, out, n);
+    NUFFT_LAUNCH("k_widen");
 }
 
 // ---------------------------------------------------------------------

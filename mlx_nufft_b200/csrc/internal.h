@@ -81,6 +81,11 @@ struct CellParams {
     double e[3];          // CELL_T3TGT: n_up/2.0
     int m[3];             // bin extent
     int nb[3];            // bins per dimension
+    // Caller-order chunking of the sort (0: off).  With chunking the sort
+    // key is (j / chunk, bin), so all subproblems of one chunk touch only
+    // that chunk's slice of the caller-ordered strengths / outputs, which
+    // stays L2-resident while it is being gathered or scattered.
+    int64_t chunk;
 };
 
 struct TileGeom {
@@ -94,6 +99,7 @@ struct TileGeom {
     int halfw;            // w / 2
     float c2w;            // (float)(2.0 / w)
     float beta;           // (float) beta
+    int keval;            // 1: polynomial weights, 0: exp/sqrt per tap
     EsPoly poly;          // ES kernel as per-tap polynomials in fr
 };
 
@@ -152,11 +158,12 @@ void device_minmax(int n, const double* const* arrs, int64_t M, double* out,
 void launch_spread(const PointSet& ps, const TileGeom& tg, int w,
                    const float2* c, int64_t cstride, int nvec,
                    float2* grid, int nvg, cudaStream_t st);
-// Interpolate nvec grids at the points into out (vector stride ostride),
-// multiplying by ps.phase when present.
+// Interpolate nvec grids (complex64, or complex128 when grid64) at the
+// points into out (vector stride ostride), multiplying by ps.phase when
+// present.
 void launch_interp(const PointSet& ps, const TileGeom& tg, int w,
-                   const float2* grid, int nvec, float2* out, int64_t ostride,
-                   int nvg, cudaStream_t st);
+                   const void* grid, bool grid64, int nvec, float2* out,
+                   int64_t ostride, int nvg, cudaStream_t st);
 // Largest dynamic shared memory a tile kernel may use (bytes).
 int tile_smem_limit();
 // Spread one group of a disjoint-support batch: point j goes to grid
@@ -167,14 +174,18 @@ void launch_spread_groups(const PointSet& ps, const TileGeom& tg, int w,
 
 // deconv.cu
 // Type-1 crop: fk[v][m] = grid[v][r(m)] * prod dec_d[m_d]   (nd.py:416-435)
+// (grid complex64, or complex128 when grid64)
 void launch_crop(int dim, const int64_t* N, const int64_t* n,
-                 const float* const* dec, const float2* grid, float2* fk,
-                 int nvec, cudaStream_t st);
+                 const float* const* dec, const void* grid, bool grid64,
+                 float2* fk, int nvec, cudaStream_t st);
 // Pad: H[v][r] = in-band ? f[v][m(r)] * prod dec_d[m_d] : 0
-// (types 2 and 3: nd.py:878-906, gpu_t3.py:629-651)
+// (types 2 and 3: nd.py:878-906, gpu_t3.py:629-651); H complex64, or
+// complex128 when grid64.
 void launch_pad(int dim, const int64_t* N, const int64_t* n,
-                const float* const* dec, const float2* f, float2* H,
-                int nvec, cudaStream_t st);
+                const float* const* dec, const float2* f, void* H,
+                bool grid64, int nvec, cudaStream_t st);
+// complex64 -> complex128 copy of n elements (fp64 FFT input)
+void launch_widen(const float2* in, double2* out, int64_t n, cudaStream_t st);
 // e^{i isign sum_c comps[c][j]}  (dfmath.py:29-54)
 void launch_expi(int ncomp, const double* const* comps, int64_t n, int isign,
                  float2* out, cudaStream_t st);

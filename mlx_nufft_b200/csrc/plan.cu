@@ -134,8 +134,13 @@ struct nufft_plan_s {
     PointSet src, tgt;
     TileGeom tg_src{}, tg_tgt{};
     int nvg_src = 1, nvg_tgt = 1;
-    float2* gspread = nullptr;   // type 3 only (nf grids)
-    float2* gfft = nullptr;      // n_up grids (types 1/2: also the spread grid)
+    // Fine grids.  gfft holds the FFT grids (complex64, or complex128 when
+    // fft64); gspread is the complex64 spreading target of type 3 (nf
+    // grids) and of type 1 when fft64 (n_up grids); otherwise type 1
+    // spreads straight into gfft.
+    bool fft64 = false;
+    float2* gspread = nullptr;
+    float2* gfft = nullptr;
     std::map<int, cufftHandle> ffts;
     bool profile = false;
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -149,7 +154,7 @@ namespace nufft_impl {
 // tiling choice per grid: bin extent m per dimension so that the tile
 // (m + w - 1)^dim of complex64 fits shared memory with room for several
 // vectors.
-TileGeom make_tile(int dim, const int64_t* n, int w, double beta) {
+TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval) {
     TileGeom tg{};
     tg.dim = dim;
     tg.ncells = 1;
@@ -157,6 +162,7 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta) {
     tg.halfw = w / 2;
     tg.c2w = (float)(2.0 / w);
     tg.beta = (float)beta;
+    tg.keval = keval ? 1 : 0;
     tg.poly = make_es_poly(w, beta);
     int m0 = dim == 1 ? 1024 : (dim == 2 ? 32 : 8);
     for (int d = 0; d < 3; ++d) {
@@ -176,15 +182,27 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta) {
     return tg;
 }
 
+// Caller-order chunk (points) of the bin sort.  In 1-D / 2-D a point touches
+// few cells, so the cost that dominates is the caller-ordered access of
+// its strength (spread) or output (interp), which a plain bin sort turns
+// into a random 8-byte scatter/gather over the whole array.  Sorting by
+// (chunk, bin) bounds the array slice in flight to ~16 MB (L2-resident);
+// the price is one extra tile load per bin per chunk, from L2.  In 3-D the
+// per-point tap work dominates and bins need all their points, so 0.
+int64_t sort_chunk(int dim) { return dim <= 2 ? (int64_t)1 << 21 : 0; }
+
+// dynamic shared memory available to a tile (kernels keep < 1 KB static)
+size_t tile_bytes_max() { return (size_t)tile_smem_limit() - 1024; }
+
 bool tile_fits(const TileGeom& tg) {
-    return (size_t)tg.tcells * sizeof(float2) <= (size_t)tile_smem_limit();
+    return (size_t)tg.tcells * sizeof(float2) <= tile_bytes_max();
 }
 
 int vectors_per_tile(const TileGeom& tg, int nbatch) {
     const size_t per = (size_t)tg.tcells * sizeof(float2);
     int nvg = (int)std::max<size_t>(1, kTileBudget / per);
-    if ((size_t)nvg * per > (size_t)tile_smem_limit())
-        nvg = (int)std::max<size_t>(1, tile_smem_limit() / per);
+    if ((size_t)nvg * per > tile_bytes_max())
+        nvg = (int)std::max<size_t>(1, tile_bytes_max() / per);
     return std::max(1, std::min(nvg, nbatch));
 }
 
@@ -230,7 +248,8 @@ cufftHandle get_fft(nufft_plan_s* p, int nv) {
     for (int d = 0; d < p->dim; ++d) n[d] = p->nup[d];
     size_t ws = 0;
     cufftResult r = cufftMakePlanMany64(h, p->dim, n, nullptr, 1, p->nupcells,
-                                        nullptr, 1, p->nupcells, CUFFT_C2C, nv,
+                                        nullptr, 1, p->nupcells,
+                                        p->fft64 ? CUFFT_Z2Z : CUFFT_C2C, nv,
                                         &ws);
     if (r != CUFFT_SUCCESS) {
         cufftDestroy(h);
@@ -240,12 +259,28 @@ cufftHandle get_fft(nufft_plan_s* p, int nv) {
     return h;
 }
 
-void run_fft(nufft_plan_s* p, float2* grid, int nv, cudaStream_t st) {
+// In-place FFT of nv fine grids (gfft), unnormalised inverse for isign > 0.
+void run_fft(nufft_plan_s* p, int nv, cudaStream_t st) {
     cufftHandle h = get_fft(p, nv);
     check_cufft(cufftSetStream(h, st), "cufftSetStream");
     const int dir = p->isign > 0 ? CUFFT_INVERSE : CUFFT_FORWARD;
-    check_cufft(cufftExecC2C(h, (cufftComplex*)grid, (cufftComplex*)grid, dir),
-                "cufftExecC2C");
+    if (p->fft64)
+        check_cufft(cufftExecZ2Z(h, (cufftDoubleComplex*)p->gfft,
+                                 (cufftDoubleComplex*)p->gfft, dir),
+                    "cufftExecZ2Z");
+    else
+        check_cufft(cufftExecC2C(h, (cufftComplex*)p->gfft,
+                                 (cufftComplex*)p->gfft, dir),
+                    "cufftExecC2C");
+}
+
+size_t fft_cell_bytes(const nufft_plan_s* p) {
+    return p->fft64 ? sizeof(double2) : sizeof(float2);
+}
+
+// Spreading target of type 1 (complex64 n_up grids).
+float2* t1_spread_grid(const nufft_plan_s* p) {
+    return p->fft64 ? p->gspread : p->gfft;
 }
 
 void alloc_grids(nufft_plan_s* p) {
@@ -253,10 +288,24 @@ void alloc_grids(nufft_plan_s* p) {
     p->gfft = nullptr;
     dfree(p->gspread);
     p->gspread = nullptr;
-    p->gfft = (float2*)dmalloc(sizeof(float2) * p->nupcells * p->nbatch, "fine grid");
+    p->gfft = (float2*)dmalloc(fft_cell_bytes(p) * p->nupcells * p->nbatch,
+                               "fine grid");
     if (p->type == 3)
         p->gspread = (float2*)dmalloc(sizeof(float2) * p->nfcells * p->nbatch,
                                       "type-3 spread grid");
+    else if (p->type == 1 && p->fft64)
+        p->gspread = (float2*)dmalloc(sizeof(float2) * p->nupcells * p->nbatch,
+                                      "type-1 spread grid");
+}
+
+// fp64 FFT when cuFFT's fp32 rounding would be amplified by the 1/phihat
+// corrections: at upsampling < 1.5 the corrections near the band edge reach
+// 1e3..1e5, and cuFFT's fp32 error (~1e-7 relative rms, several times that
+// of an fp32 FFT with accurate twiddles) then dominates the result.
+bool want_fft64(const nufft_plan_s* p, double sigma_inner) {
+    if (p->opts.fft_prec == 2) return true;
+    if (p->opts.fft_prec == 1) return false;
+    return sigma_inner < 1.5 && p->eps < 1e-4;
 }
 
 void record(nufft_plan_s* p, int i, cudaStream_t st) {
@@ -283,6 +332,7 @@ void create_t12(nufft_plan_s* p) {
     kernel_params(p->eps, p->sigma, &p->w, &p->beta);
     p->w2 = p->w;
     p->beta2 = p->beta;
+    p->fft64 = want_fft64(p, p->sigma);
     p->K = 1;
     p->nupcells = 1;
     for (int d = 0; d < p->dim; ++d) {
@@ -306,7 +356,7 @@ void create_t12(nufft_plan_s* p) {
         }
         upload_dec(p, d, v);
     }
-    p->tg_src = make_tile(p->dim, p->nup, p->w, p->beta);
+    p->tg_src = make_tile(p->dim, p->nup, p->w, p->beta, p->opts.kerevalmeth);
     p->nvg_src = vectors_per_tile(p->tg_src, p->nbatch);
     alloc_grids(p);
     p->sized = true;
@@ -328,6 +378,7 @@ void setpts_t12(nufft_plan_s* p, int64_t M, const double* const* xs,
     }
     const bool tiled = want_tiled(p, M, p->tg_src);
     const bool sort = tiled || p->opts.sort_points;
+    cp.chunk = tiled ? sort_chunk(p->dim) : 0;
     PhaseParams pp{};
     build_pointset(&p->src, cp, M, xs, sort, tiled,
                    p->type == 1 ? kMsubSpread : kMsubInterp, pp, p->d_err, st);
@@ -355,6 +406,7 @@ void create_t3(nufft_plan_s* p) {
         p->w2 = ns;
         p->beta2 = 0.97 * kPi * (1.0 - 1.0 / (2.0 * si)) * ns;
     }
+    p->fft64 = want_fft64(p, p->sigma_in);
     std::vector<double> dq, aq;
     kernel_ft_nodes(p->beta, p->w, &dq, &aq);
     p->d_ftd = (double*)dmalloc(sizeof(double) * dq.size(), "phihat nodes");
@@ -406,9 +458,9 @@ void size_t3(nufft_plan_s* p, const double* slo, const double* shi) {
         destroy_ffts(p);
         alloc_grids(p);
     }
-    p->tg_src = make_tile(p->dim, p->nf, p->w, p->beta);
+    p->tg_src = make_tile(p->dim, p->nf, p->w, p->beta, p->opts.kerevalmeth);
     p->nvg_src = vectors_per_tile(p->tg_src, p->nbatch);
-    p->tg_tgt = make_tile(p->dim, p->nup, p->w2, p->beta2);
+    p->tg_tgt = make_tile(p->dim, p->nup, p->w2, p->beta2, p->opts.kerevalmeth);
     p->nvg_tgt = vectors_per_tile(p->tg_tgt, p->nbatch);
     p->sized = true;
 }
@@ -453,6 +505,7 @@ void set_sources_t3(nufft_plan_s* p, int64_t M, const double* const* xs,
     for (int d = 0; d < p->dim; ++d) pp.D[d] = p->D[d];
     const bool tiled = want_tiled(p, M, p->tg_src);
     const bool sort = tiled || p->opts.sort_points;
+    cp.chunk = tiled ? sort_chunk(p->dim) : 0;
     build_pointset(&p->src, cp, M, xs, sort, tiled, kMsubSpread, pp, p->d_err, st);
     check_err_flag(p, st);
 }
@@ -513,6 +566,7 @@ void setpts_t3(nufft_plan_s* p, int64_t M, const double* const* xs, int64_t N,
     pp.nq = 128;
     const bool tiled = want_tiled(p, N, p->tg_tgt);
     const bool sort = tiled || p->opts.sort_points;
+    cp.chunk = tiled ? sort_chunk(p->dim) : 0;
     build_pointset(&p->tgt, cp, N, ss, sort, tiled, kMsubInterp, pp, p->d_err, st);
     check_err_flag(p, st);
     p->Ntgt = N;
@@ -524,12 +578,12 @@ void setpts_t3(nufft_plan_s* p, int64_t M, const double* const* xs, int64_t N,
 // ---------------------------------------------------------------------
 void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
                    int stage, cudaStream_t st) {
-    const size_t gbytes = sizeof(float2) * p->nupcells * nv;
     if (p->type == 1) {
+        float2* sg = t1_spread_grid(p);
         if (stage == NUFFT_STAGE_ALL || stage == NUFFT_STAGE_SPREAD) {
             record(p, 0, st);
-            NUFFT_CUDA(cudaMemsetAsync(p->gfft, 0, gbytes, st));
-            launch_spread(p->src, p->tg_src, p->w, in, p->src.M, nv, p->gfft,
+            NUFFT_CUDA(cudaMemsetAsync(sg, 0, sizeof(float2) * p->nupcells * nv, st));
+            launch_spread(p->src, p->tg_src, p->w, in, p->src.M, nv, sg,
                           p->nvg_src, st);
             record(p, 1, st);
         }
@@ -538,31 +592,34 @@ void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
                 record(p, 0, st);
                 record(p, 1, st);
             }
-            run_fft(p, p->gfft, nv, st);
+            if (p->fft64) launch_widen(sg, (double2*)p->gfft, p->nupcells * nv, st);
+            run_fft(p, nv, st);
             record(p, 2, st);
-            launch_crop(p->dim, p->N, p->nup, p->dec, p->gfft, out, nv, st);
+            launch_crop(p->dim, p->N, p->nup, p->dec, p->gfft, p->fft64, out, nv,
+                        st);
             record(p, 3, st);
         }
     } else if (p->type == 2) {
         record(p, 0, st);
-        launch_pad(p->dim, p->N, p->nup, p->dec, in, p->gfft, nv, st);
+        launch_pad(p->dim, p->N, p->nup, p->dec, in, p->gfft, p->fft64, nv, st);
         record(p, 1, st);
-        run_fft(p, p->gfft, nv, st);
+        run_fft(p, nv, st);
         record(p, 2, st);
-        launch_interp(p->src, p->tg_src, p->w, p->gfft, nv, out, p->src.M,
-                      p->nvg_src, st);
+        launch_interp(p->src, p->tg_src, p->w, p->gfft, p->fft64, nv, out,
+                      p->src.M, p->nvg_src, st);
         record(p, 3, st);
     } else {
         record(p, 0, st);
         NUFFT_CUDA(cudaMemsetAsync(p->gspread, 0, sizeof(float2) * p->nfcells * nv, st));
         launch_spread(p->src, p->tg_src, p->w, in, p->src.M, nv, p->gspread,
                       p->nvg_src, st);
-        launch_pad(p->dim, p->nf, p->nup, p->dec, p->gspread, p->gfft, nv, st);
+        launch_pad(p->dim, p->nf, p->nup, p->dec, p->gspread, p->gfft, p->fft64,
+                   nv, st);
         record(p, 1, st);
-        run_fft(p, p->gfft, nv, st);
+        run_fft(p, nv, st);
         record(p, 2, st);
-        launch_interp(p->tgt, p->tg_tgt, p->w2, p->gfft, nv, out, p->Ntgt,
-                      p->nvg_tgt, st);
+        launch_interp(p->tgt, p->tg_tgt, p->w2, p->gfft, p->fft64, nv, out,
+                      p->Ntgt, p->nvg_tgt, st);
         record(p, 3, st);
     }
     p->ev_recorded = p->profile;
@@ -575,7 +632,9 @@ void ensure_batch(nufft_plan_s* p, int nvec) {
     if (nvec <= p->nbatch || p->opts.max_batch > 0) return;
     size_t free_b = 0, tot = 0;
     NUFFT_CUDA(cudaMemGetInfo(&free_b, &tot));
-    const size_t per = sizeof(float2) * (size_t)(p->nupcells + (p->type == 3 ? p->nfcells : 0));
+    size_t per = fft_cell_bytes(p) * (size_t)p->nupcells;
+    if (p->type == 3) per += sizeof(float2) * (size_t)p->nfcells;
+    else if (p->type == 1 && p->fft64) per += sizeof(float2) * (size_t)p->nupcells;
     const size_t have = per * (size_t)p->nbatch;
     const int64_t cap = (int64_t)((free_b / 2 + have) / per);
     const int nb = (int)std::min<int64_t>(nvec, std::max<int64_t>(cap, p->nbatch));
@@ -638,6 +697,7 @@ void nufft_default_opts(nufft_opts* o) {
     o->prec = NUFFT_PREC_CRIT64;
     o->method = NUFFT_METHOD_AUTO;
     o->sort_points = 1;
+    o->kerevalmeth = 1;
 }
 
 int nufft_plan_create(int type, int dim, const int64_t* n_modes, int n_trans,
@@ -774,7 +834,9 @@ int nufft_execute(nufft_plan_t p, const void* in, void* out, int nvec,
 int nufft_get_grid(nufft_plan_t p, void** grid, int64_t* n_complex) {
     return guarded([&] {
         if (!p) fail(NUFFT_ERR_ARG, "NULL plan");
-        if (grid) *grid = p->gfft;
+        // the complex64 spreading target (type 1: what SPREAD leaves for a
+        // cross-GPU reduction before FINISH)
+        if (grid) *grid = p->type == 1 ? t1_spread_grid(p) : p->gfft;
         if (n_complex) *n_complex = p->nupcells * p->nbatch;
     });
 }
@@ -796,13 +858,15 @@ int nufft_execute_disjoint(nufft_plan_t p, const void* c, const int32_t* groups,
         try {
             for (int g0 = 0; g0 < ngroups; g0 += p->nbatch) {
                 const int ng = std::min(p->nbatch, ngroups - g0);
-                NUFFT_CUDA(cudaMemsetAsync(p->gfft, 0, sizeof(float2) * p->nupcells * ng, st));
+                float2* sg = t1_spread_grid(p);
+                NUFFT_CUDA(cudaMemsetAsync(sg, 0, sizeof(float2) * p->nupcells * ng, st));
                 // labels relative to this window; out-of-window -> -1
                 window_labels(groups, p->src.M, g0, ng, shifted, st);
-                launch_spread_groups(p->src, p->tg_src, p->w, fc, shifted, p->gfft, st);
-                run_fft(p, p->gfft, ng, st);
-                launch_crop(p->dim, p->N, p->nup, p->dec, p->gfft, fo + (int64_t)g0 * p->K,
-                            ng, st);
+                launch_spread_groups(p->src, p->tg_src, p->w, fc, shifted, sg, st);
+                if (p->fft64) launch_widen(sg, (double2*)p->gfft, p->nupcells * ng, st);
+                run_fft(p, ng, st);
+                launch_crop(p->dim, p->N, p->nup, p->dec, p->gfft, p->fft64,
+                            fo + (int64_t)g0 * p->K, ng, st);
             }
         } catch (...) {
             NUFFT_CUDA(cudaStreamSynchronize(st));
@@ -866,7 +930,8 @@ int nufft_plan_get_info(nufft_plan_t p, nufft_plan_info* info) {
         info->tiled = p->src.tiled ? 1 : 0;
         info->nsub = p->src.nsub;
         info->nsub_tgt = p->tgt.nsub;
-        int64_t b = sizeof(float2) * (p->nupcells * p->nbatch);
+        int64_t b = (int64_t)fft_cell_bytes(p) * (p->nupcells * p->nbatch);
+        if (p->type == 1 && p->fft64) b += sizeof(float2) * p->nupcells * p->nbatch;
         if (p->type == 3) b += sizeof(float2) * p->nfcells * p->nbatch;
         b += p->src.cap * (8 * p->dim + 4 + (p->src.phase ? 8 : 0));
         b += p->tgt.cap * (8 * p->dim + 4 + (p->tgt.phase ? 8 : 0));

@@ -113,7 +113,7 @@ __global__ void k_bin_count(int64_t M, Coords X, CellParams cp,
     int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (j >= M) return;
     bool bad = false;
-    uint32_t key = 0;
+    uint32_t key = cp.chunk ? (uint32_t)(j / cp.chunk) : 0u;
 #pragma unroll
     for (int d = 0; d < DIM; ++d) {
         int i1, ib;
@@ -181,17 +181,20 @@ __global__ void k_sub_count(const uint32_t* count, int64_t nbins, int msub,
     nsubs[b] = (count[b] + (uint32_t)msub - 1u) / (uint32_t)msub;
 }
 
+// Subproblem table: one entry per <= msub points of a sort key; the entry
+// carries the spatial bin (key mod the number of spatial bins).
 __global__ void k_sub_fill(const uint32_t* count, const uint32_t* start,
-                           const uint32_t* subofs, int64_t nbins, int msub,
-                           int4* subs) {
+                           const uint32_t* subofs, int64_t nbins,
+                           int64_t nbins_spatial, int msub, int4* subs) {
     int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (b >= nbins) return;
     uint32_t n = count[b];
     uint32_t k0 = subofs[b];
+    const int spatial = (int)(b % nbins_spatial);
     for (uint32_t k = 0; k * (uint32_t)msub < n; ++k) {
         uint32_t s = start[b] + k * (uint32_t)msub;
         uint32_t c = min((uint32_t)msub, n - k * (uint32_t)msub);
-        subs[k0 + k] = make_int4((int)s, (int)c, (int)b, 0);
+        subs[k0 + k] = make_int4((int)s, (int)c, spatial, 0);
     }
 }
 
@@ -336,9 +339,11 @@ void build_impl(PointSet* ps, const CellParams& cp, int64_t M,
             M, X, cp, ps->cell[0], ps->cell[1], ps->cell[2], d_err);
         NUFFT_LAUNCH("k_cells_direct");
     } else {
-        int64_t nbins = 1;
-        for (int d = 0; d < DIM; ++d) nbins *= cp.nb[d];
-        if (nbins > (int64_t)0xffffffffLL) fail(-1, "too many bins");
+        int64_t nbins_sp = 1;
+        for (int d = 0; d < DIM; ++d) nbins_sp *= cp.nb[d];
+        const int64_t nchunks = cp.chunk ? (M + cp.chunk - 1) / cp.chunk : 1;
+        const int64_t nbins = nbins_sp * nchunks;
+        if (nbins > (int64_t)0x7fffffffLL) fail(-1, "too many bins");
         uint32_t* key_of = (uint32_t*)dmalloc(4 * M, "sort keys");
         uint32_t* rank_of = (uint32_t*)dmalloc(4 * M, "sort ranks");
         uint32_t* count = (uint32_t*)dmalloc(4 * (nbins + 1), "bin counts");
@@ -374,8 +379,8 @@ void build_impl(PointSet* ps, const CellParams& cp, int64_t M,
                                           "subproblems");
                 ps->subcap = std::max<int64_t>(h_tot, 1);
             }
-            k_sub_fill<<<gb, 256, 0, st>>>(count, start, subofs, nbins, msub,
-                                           ps->subs);
+            k_sub_fill<<<gb, 256, 0, st>>>(count, start, subofs, nbins,
+                                           nbins_sp, msub, ps->subs);
             NUFFT_LAUNCH("k_sub_fill");
             ps->nsub = h_tot;
             NUFFT_CUDA(cudaStreamSynchronize(st));

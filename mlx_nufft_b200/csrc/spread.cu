@@ -49,13 +49,19 @@ int persistent_grid(const void* kernel, size_t smem, int64_t work) {
 
 void ensure_smem(const void* kernel, size_t bytes) {
     static std::mutex mu;
-    static std::set<const void*> raised;
+    static std::map<const void*, size_t> raised;   // kernel -> limit set
     if (bytes <= 48 * 1024) return;
     std::lock_guard<std::mutex> lk(mu);
-    if (raised.count(kernel)) return;
+    auto it = raised.find(kernel);
+    if (it != raised.end() && it->second >= bytes) return;
+    // the dynamic limit excludes the kernel's static shared memory
+    cudaFuncAttributes fa{};
+    NUFFT_CUDA(cudaFuncGetAttributes(&fa, kernel));
+    const size_t cap = (size_t)tile_smem_limit() - fa.sharedSizeBytes;
+    if (bytes > cap) fail(-1, "tile does not fit in shared memory");
     NUFFT_CUDA(cudaFuncSetAttribute(
-        kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tile_smem_limit()));
-    raised.insert(kernel);
+        kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cap));
+    raised[kernel] = cap;
 }
 
 namespace {

@@ -57,6 +57,44 @@ __device__ __forceinline__ void es_weights(float fr, const EsPoly& P,
         for (int l = 0; l < W; ++l) wt[l] = fmaf(wt[l], t, P.c[k][l]);
 }
 
+// Weights by the plan's evaluation method: per-tap polynomials (keval 1)
+// or the exact exp/sqrt form of the reference (keval 0).
+template <int W>
+__device__ __forceinline__ void kernel_weights(float fr, const TileGeom& tg,
+                                               float* wt) {
+    if (tg.keval) {
+        es_weights<W>(fr, tg.poly, wt);
+    } else {
+#pragma unroll
+        for (int l = 0; l < W; ++l)
+            wt[l] = es_weight((float)l - fr, tg.c2w, tg.beta);
+    }
+}
+
+// L2 evict-last policy for scattered output stores: a sorted-order interp
+// writes each caller-order output sector from several subproblems at
+// different times; keeping those lines resident lets L2 merge the partial
+// sectors instead of write-allocating each one from DRAM.
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;"
+                 : "=l"(pol));
+    return pol;
+}
+
+__device__ __forceinline__ void st_keep(float2* p, float2 v, uint64_t pol) {
+    asm volatile("st.global.L2::cache_hint.v2.f32 [%0], {%1, %2}, %3;"
+                 :: "l"(p), "f"(v.x), "f"(v.y), "l"(pol) : "memory");
+}
+
+// Fine-grid element loads: the grid is complex64 (float2) or, with the
+// fp64 FFT mode, complex128 (double2); either way the taps are fp32.
+__device__ __forceinline__ float2 load_cell(const float2* p) { return __ldg(p); }
+__device__ __forceinline__ float2 load_cell(const double2* p) {
+    const double2 v = __ldg(p);
+    return make_float2((float)v.x, (float)v.y);
+}
+
 // Cyclic left rotation by one (compile-time indices only).
 template <int W, typename T>
 __device__ __forceinline__ void rotate(T* a) {
@@ -124,7 +162,7 @@ __device__ __forceinline__ bool point_weights(const CellPtrs& cells, int64_t j,
         int2 cl = __ldg(cells.d[d] + j);
         l0[d] = cl.x - o[d];
         ok &= (unsigned)l0[d] < (unsigned)tg.m[d];
-        es_weights<W>(__int_as_float(cl.y), tg.poly, wgt[d]);
+        kernel_weights<W>(__int_as_float(cl.y), tg, wgt[d]);
     }
     return ok;
 }
@@ -305,7 +343,7 @@ k_spread_tiled(const float2* __restrict__ c, int64_t cstride, int nvg,
                 for (int d = 0; d < DIM; ++d) {
                     l0[d] = cl[u][d].x - o[d];
                     ok &= (unsigned)l0[d] < (unsigned)tg.m[d];
-                    es_weights<W>(__int_as_float(cl[u][d].y), tg.poly, wgt[d]);
+                    kernel_weights<W>(__int_as_float(cl[u][d].y), tg, wgt[d]);
                 }
                 if (!ok) continue;
                 for (int v = 0; v < nvg; ++v) {
@@ -332,9 +370,9 @@ k_spread_tiled(const float2* __restrict__ c, int64_t cstride, int nvg,
 
 // --------------------------------------------------------------------
 // tiled interp: out[v][perm j] = phase_j * sum taps tile[v] * psi-tensor
-template <int DIM, int W>
+template <int DIM, int W, typename G>
 __global__ void __launch_bounds__(256)
-k_interp_tiled(const float2* __restrict__ grid, int nvg,
+k_interp_tiled(const G* __restrict__ grid, int nvg,
                const uint32_t* __restrict__ perm, CellPtrs cells,
                const float2* __restrict__ phase, const int4* __restrict__ subs,
                int nsub, int* __restrict__ sched, float2* __restrict__ out,
@@ -343,6 +381,7 @@ k_interp_tiled(const float2* __restrict__ grid, int nvg,
     __shared__ int s_sub;
     constexpr int U = batch_u<DIM>();
     const int T = tg.tcells;
+    const uint64_t pol = l2_evict_last_policy();
     for (;;) {
         const int sub = next_subproblem(sched, &s_sub);
         if (sub >= nsub) break;
@@ -353,7 +392,7 @@ k_interp_tiled(const float2* __restrict__ grid, int nvg,
         for (int q = threadIdx.x; q < T; q += blockDim.x) {
             const int64_t g = tile_to_global<DIM>(q, o, tg);
             for (int v = 0; v < nvg; ++v)
-                tile[v * T + q] = __ldg(grid + v * tg.ncells + g);
+                tile[v * T + q] = load_cell(grid + v * tg.ncells + g);
         }
         __syncthreads();
         for (int base = 0; base < cnt; base += U * blockDim.x) {
@@ -379,7 +418,7 @@ k_interp_tiled(const float2* __restrict__ grid, int nvg,
                 for (int d = 0; d < DIM; ++d) {
                     l0[d] = cl[u][d].x - o[d];
                     ok &= (unsigned)l0[d] < (unsigned)tg.m[d];
-                    es_weights<W>(__int_as_float(cl[u][d].y), tg.poly, wgt[d]);
+                    kernel_weights<W>(__int_as_float(cl[u][d].y), tg, wgt[d]);
                 }
                 for (int v = 0; v < nvg; ++v) {
                     float2 acc = make_float2(0.0f, 0.0f);
@@ -387,7 +426,10 @@ k_interp_tiled(const float2* __restrict__ grid, int nvg,
                         acc = tile_gather<DIM, W>(tile + v * T, tg, l0, wgt);
                         if (phase) acc = cmul(acc, ph[u]);
                     }
-                    out[v * ostride + dst[u]] = acc;
+                    if (perm)
+                        st_keep(out + v * ostride + dst[u], acc, pol);
+                    else
+                        out[v * ostride + dst[u]] = acc;
                 }
             }
         }
@@ -406,7 +448,7 @@ __device__ __forceinline__ void global_taps(const CellPtrs& cells, int64_t j,
 #pragma unroll
     for (int d = 0; d < DIM; ++d) {
         int2 cl = __ldg(cells.d[d] + j);
-        es_weights<W>(__int_as_float(cl.y), tg.poly, wgt[d]);
+        kernel_weights<W>(__int_as_float(cl.y), tg, wgt[d]);
 #pragma unroll
         for (int l = 0; l < W; ++l) idx[d][l] = wrap1(cl.x + l, tg.n[d]);
     }
@@ -452,8 +494,8 @@ __device__ __forceinline__ void global_add(float2* gv, const TileGeom& tg,
     }
 }
 
-template <int DIM, int W>
-__device__ __forceinline__ float2 global_gather(const float2* gv,
+template <int DIM, int W, typename G>
+__device__ __forceinline__ float2 global_gather(const G* gv,
                                                 const TileGeom& tg,
                                                 float (&wgt)[DIM][W],
                                                 int (&idx)[DIM][W]) {
@@ -461,7 +503,7 @@ __device__ __forceinline__ float2 global_gather(const float2* gv,
     if constexpr (DIM == 1) {
 #pragma unroll
         for (int a = 0; a < W; ++a) {
-            const float2 g = __ldg(gv + idx[0][a]);
+            const float2 g = load_cell(gv + idx[0][a]);
             acc.x = fmaf(g.x, wgt[0][a], acc.x);
             acc.y = fmaf(g.y, wgt[0][a], acc.y);
         }
@@ -472,7 +514,7 @@ __device__ __forceinline__ float2 global_gather(const float2* gv,
             float2 s = make_float2(0.0f, 0.0f);
 #pragma unroll
             for (int b = 0; b < W; ++b) {
-                const float2 g = __ldg(gv + row + idx[1][b]);
+                const float2 g = load_cell(gv + row + idx[1][b]);
                 s.x = fmaf(g.x, wgt[1][b], s.x);
                 s.y = fmaf(g.y, wgt[1][b], s.y);
             }
@@ -486,11 +528,11 @@ __device__ __forceinline__ float2 global_gather(const float2* gv,
             float2 sa = make_float2(0.0f, 0.0f);
 #pragma unroll
             for (int b = 0; b < W; ++b) {
-                const float2* row = gv + (plane + idx[1][b]) * tg.n[2];
+                const G* row = gv + (plane + idx[1][b]) * tg.n[2];
                 float2 s = make_float2(0.0f, 0.0f);
 #pragma unroll
                 for (int k = 0; k < W; ++k) {
-                    const float2 g = __ldg(row + idx[2][k]);
+                    const float2 g = load_cell(row + idx[2][k]);
                     s.x = fmaf(g.x, wgt[2][k], s.x);
                     s.y = fmaf(g.y, wgt[2][k], s.y);
                 }
@@ -526,9 +568,9 @@ k_spread_global(const float2* __restrict__ c, int64_t cstride, int nvec,
     }
 }
 
-template <int DIM, int W>
+template <int DIM, int W, typename G>
 __global__ void __launch_bounds__(256)
-k_interp_global(const float2* __restrict__ grid, int nvec,
+k_interp_global(const G* __restrict__ grid, int nvec,
                 const uint32_t* __restrict__ perm, CellPtrs cells,
                 const float2* __restrict__ phase, int64_t M,
                 float2* __restrict__ out, int64_t ostride, TileGeom tg) {
@@ -540,7 +582,7 @@ k_interp_global(const float2* __restrict__ grid, int nvec,
     global_taps<DIM, W>(cells, j, tg, wgt, idx);
     const float2 ph = phase ? __ldg(phase + j) : make_float2(1.0f, 0.0f);
     for (int v = 0; v < nvec; ++v) {
-        float2 acc = global_gather<DIM, W>(grid + v * tg.ncells, tg, wgt, idx);
+        float2 acc = global_gather<DIM, W, G>(grid + v * tg.ncells, tg, wgt, idx);
         if (phase) acc = cmul(acc, ph);
         out[v * ostride + dst] = acc;
     }

@@ -39,7 +39,7 @@ class _PointsND:
     _TYPE = 0
 
     def __init__(self, x, n_modes, eps, isign, upsampfac, prec, sort_points,
-                 spread_method):
+                 spread_method, kerevalmeth=1):
         if prec not in ("fp32", "crit64"):
             raise ValueError("prec must be 'fp32' or 'crit64'")
         x = _coords_tuple(x)
@@ -71,7 +71,8 @@ class _PointsND:
         self._method = spread_method
         self._plan = NativePlan(self._TYPE, self.dim, self.N, 1, eps,
                                 self.isign, upsampfac=upsampfac, prec=prec,
-                                method=spread_method, sort_points=sort_points)
+                                method=spread_method, sort_points=sort_points,
+                                kerevalmeth=kerevalmeth)
         self._perm_cache = None
         self._set_points(x)
 
@@ -145,9 +146,10 @@ class Type1PlanND(_PointsND):
     _TYPE = 1
 
     def __init__(self, x, n_modes, eps=1e-6, isign=+1, upsampfac=2.0,
-                 prec="crit64", sort_points=True, spread_method="auto"):
+                 prec="crit64", sort_points=True, spread_method="auto",
+                 kerevalmeth=1):
         super().__init__(x, n_modes, eps, isign, upsampfac, prec, sort_points,
-                         spread_method)
+                         spread_method, kerevalmeth)
         if spread_method == "od" and not self._od:
             raise ValueError("OD spreading not applicable to this geometry")
 
@@ -207,9 +209,10 @@ class Type2PlanND(_PointsND):
     _TYPE = 2
 
     def __init__(self, x, n_modes, eps=1e-6, isign=-1, upsampfac=2.0,
-                 prec="crit64", sort_points=False, spread_method="auto"):
+                 prec="crit64", sort_points=False, spread_method="auto",
+                 kerevalmeth=1):
         super().__init__(x, n_modes, eps, isign, upsampfac, prec, sort_points,
-                         spread_method)
+                         spread_method, kerevalmeth)
         if spread_method == "od" and not self._od:
             raise ValueError("OD interp not applicable to this geometry")
 

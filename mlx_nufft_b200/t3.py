@@ -33,7 +33,8 @@ PI = np.pi
 class Type3Plan:
     def __init__(self, x, s, eps=1e-5, isign=+1, upsampfac=1.25,
                  prec="crit64", sigma_inner=None, sort_points=True,
-                 low_mem=None, source_extent=None, fft_backend="mlx"):
+                 low_mem=None, source_extent=None, fft_backend="mlx",
+                 kerevalmeth=1):
         assert prec in ("fp32", "coords64", "phases64", "crit64")
         assert fft_backend in ("mlx", "cufft", "vkfft")
         if fft_backend == "vkfft":
@@ -60,7 +61,8 @@ class Type3Plan:
         self._plan = NativePlan(3, self.dim, None, 1, eps, self.isign,
                                 upsampfac=upsampfac, sigma_inner=sigma_inner,
                                 prec=prec, sort_points=sort_points,
-                                source_extent=source_extent)
+                                source_extent=source_extent,
+                                kerevalmeth=kerevalmeth)
         dev = self._plan.device
         xt = [as_f64(v, dev) for v in xs]
         st = [as_f64(v, dev) for v in ss]
