@@ -11,7 +11,7 @@ plus the native plan classes (Type1PlanND, Type2PlanND, Type3Plan, the legacy
 Type1Plan / Type2Plan) and expi.  Every transform runs in the native library
 libnufft_b200.so (hand-written CUDA + cuFFT, reached through its C ABI,
 include/nufft_b200.h); importing this package fails if that library has not
-been built (`python -m mlx_nufft_b200.build`).  Inputs may be numpy arrays or
+been built (`python mlx_nufft_b200/build.py`).  Inputs may be numpy arrays or
 torch tensors; results are numpy by default or torch CUDA tensors with
 return_np=False.
 """

@@ -2,7 +2,7 @@
 
 Loading is strict: if the shared library is missing the import fails with an
 explicit error -- there is no CPU or pure-Python fallback for any transform.
-Build it with ``python -m mlx_nufft_b200.build``.
+Build it with ``python mlx_nufft_b200/build.py``.
 """
 
 import ctypes
@@ -127,7 +127,7 @@ def _load():
     if not os.path.exists(LIB_PATH):
         raise ImportError(
             f"mlx_nufft_b200: native library {LIB_PATH} is missing; build it "
-            "with `python -m mlx_nufft_b200.build` (nvcc, sm_100a). There is "
+            "with `python mlx_nufft_b200/build.py` (nvcc, sm_100a). There is "
             "no CPU fallback.")
     lib = ctypes.CDLL(LIB_PATH)
     for name, (res, args) in _PROTOS.items():

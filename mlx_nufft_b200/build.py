@@ -1,6 +1,8 @@
 """Build libnufft_b200.so (sm_100a) in-tree with nvcc.
 
-    python -m mlx_nufft_b200.build        # or: python mlx_nufft_b200/build.py
+    python mlx_nufft_b200/build.py   [--force] [--ptxas-v]
+
+(run it as a script: importing the package needs the built library).
 
 Each CUDA / C++ source under csrc/ is compiled to an object in
 mlx_nufft_b200/_build/ (in parallel, skipped when up to date) and linked

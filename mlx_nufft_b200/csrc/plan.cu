@@ -15,6 +15,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -150,6 +151,13 @@ struct nufft_plan_s {
 
 namespace nufft_impl {
 
+// Integer tuning override from the environment (NUFFT_BIN_1D,
+// NUFFT_SORT_CHUNK_LOG2); the default when unset.
+int env_int(const char* name, int dflt) {
+    const char* v = std::getenv(name);
+    return (v && *v) ? std::atoi(v) : dflt;
+}
+
 // ----------------------------------------------------------------------
 // tiling choice per grid: bin extent m per dimension so that the tile
 // (m + w - 1)^dim of complex64 fits shared memory with room for several
@@ -164,7 +172,8 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval) {
     tg.beta = (float)beta;
     tg.keval = keval ? 1 : 0;
     tg.poly = make_es_poly(w, beta);
-    int m0 = dim == 1 ? 1024 : (dim == 2 ? 32 : 8);
+    static const int m1d = env_int("NUFFT_BIN_1D", 1024);
+    int m0 = dim == 1 ? m1d : (dim == 2 ? 32 : 8);
     for (int d = 0; d < 3; ++d) {
         if (d < dim) {
             tg.n[d] = (int)n[d];
@@ -189,7 +198,11 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval) {
 // (chunk, bin) bounds the array slice in flight to ~16 MB (L2-resident);
 // the price is one extra tile load per bin per chunk, from L2.  In 3-D the
 // per-point tap work dominates and bins need all their points, so 0.
-int64_t sort_chunk(int dim) { return dim <= 2 ? (int64_t)1 << 21 : 0; }
+// NUFFT_SORT_CHUNK_LOG2 overrides the default (tuning; 0 disables).
+int64_t sort_chunk(int dim) {
+    static const int lg = env_int("NUFFT_SORT_CHUNK_LOG2", 21);
+    return (dim <= 2 && lg > 0) ? (int64_t)1 << lg : 0;
+}
 
 // dynamic shared memory available to a tile (kernels keep < 1 KB static)
 size_t tile_bytes_max() { return (size_t)tile_smem_limit() - 1024; }
