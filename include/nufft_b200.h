@@ -190,6 +190,45 @@ int nufft_debug_points(nufft_plan_t plan, int which, int32_t* i1, float* fr,
 int nufft_expi(int ncomp, const double* const* comps, int64_t n, int isign,
                void* out, void* stream);
 
+/* ---- interpolation without device allocation ------------------------- */
+/* Size of the device scratch array behind nufft_interp_noalloc: 16 MiB,
+ * held by every GPU that loads this library until the process exits. */
+#define NUFFT_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* Type-2 interpolation stage that allocates no device memory.  No
+ * counterpart in the reference.  For callers that must not allocate device
+ * memory themselves or through this library -- e.g. code running inside a
+ * host framework that owns the GPU's memory budget through its own
+ * allocator and treats any other allocation as an error, or a latency-
+ * critical loop that cannot afford cudaMalloc / cudaFree, which may
+ * synchronise the whole device.  Plans allocate at create / setpts; this
+ * entry point does not.
+ *
+ * Computes, on the current CUDA device and asynchronously on `stream`,
+ *   out[j] = sum over the w^dim taps of psi(taps) * grid[(i1 + l) mod n]
+ * for the M points (x, y, z) (fp64, folded mod 2*pi onto the grid spacing
+ * 2*pi / n_grid[d]), with the ES kernel (w, beta) = nufft_kernel_params(eps,
+ * upsampfac) evaluated in its exp/sqrt form.  `grid` is a complex64 fine
+ * grid of n_grid[0] x .. x n_grid[dim-1] cells (C order, FFT order) -- e.g.
+ * the grid a type-2 plan with the same eps / upsampfac has just
+ * transformed (nufft_get_grid); `out` is complex64[M] in caller order.
+ * Each n_grid[d] must be in [2w, 2^31).
+ *
+ * Scratch: the points' cell indices and fractions (8 bytes per point per
+ * dimension) live in one static device array of NUFFT_NOALLOC_SCRATCH_BYTES,
+ * so M * dim may not exceed NUFFT_NOALLOC_SCRATCH_BYTES / 8 (2,097,152);
+ * larger requests return NUFFT_ERR_ARG.  Every call on a device shares the
+ * array and it keeps the last call's contents (each call rewrites all it
+ * reads, nothing needs clearing): calls that overlap on the GPU (different
+ * streams, or threads without ordering) race and corrupt each other's
+ * results -- order them on one stream.  The first call on each device looks
+ * up the array's device address (cudaGetSymbolAddress); make that first call
+ * before any stream capture.  Non-finite coordinates are evaluated as 0. */
+int nufft_interp_noalloc(int dim, const int64_t* n_grid, double eps,
+                         double upsampfac, const void* grid, int64_t M,
+                         const double* x, const double* y, const double* z,
+                         void* out, void* stream);
+
 /* ---- host-side numerics (no GPU needed) ------------------------------ */
 /* mlx_nufft/sizing.py:28-50 */
 int nufft_kernel_params(double eps, double upsampfac, int* w, double* beta);

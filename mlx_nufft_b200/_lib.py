@@ -105,6 +105,10 @@ _PROTOS = {
     "nufft_expi": (ctypes.c_int, [
         ctypes.c_int, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int64,
         ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
+    "nufft_interp_noalloc": (ctypes.c_int, [
+        ctypes.c_int, c_int64_p, ctypes.c_double, ctypes.c_double,
+        ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "nufft_kernel_params": (ctypes.c_int, [
         ctypes.c_double, ctypes.c_double, ctypes.POINTER(ctypes.c_int),
         c_double_p]),

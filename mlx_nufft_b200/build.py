@@ -24,7 +24,7 @@ LIB = os.path.join(HERE, "libnufft_b200.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 SOURCES = ["sizing.cpp", "points.cu", "spread.cu", "interp.cu", "deconv.cu",
-           "plan.cu"]
+           "plan.cu", "noalloc.cu"]
 
 
 def _cuda_home():
