@@ -16,7 +16,7 @@ events and the algorithmic bytes of the stage), `e2e` (same metric through
 the public API from pinned host memory with the H2D / D2H copies timed),
 `cpu_baseline` (the CPU oracle port on a bounded sample, rank 0),
 `gpu_launches` (own kernels launched in the timed region), `clocks`
-(nvidia-smi samples taken during the timed region).
+(NVML samples taken during the timed region).
 
 --impl reference times the CPU port of the reference algorithm
 (oracle/port.py; the reference itself has no CPU type-1/2 path and its Metal
@@ -28,7 +28,6 @@ import json
 import os
 import re
 import statistics
-import subprocess
 import sys
 import time
 
@@ -46,7 +45,7 @@ UNIT = "NU pts/s"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", type=int, default=2)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
@@ -66,54 +65,78 @@ def peaks():
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons of this rank's GPU, sampled through
+    NVML on a background thread every `period` seconds between start() and
+    stop() (stop() takes one last sample before returning)."""
 
-    def __init__(self, index):
-        self.index = index
-        self.proc = None
+    REASONS = (("sw_power_cap", 0x4), ("hw_slowdown", 0x8),
+               ("sw_thermal_slowdown", 0x20), ("hw_thermal_slowdown", 0x40),
+               ("hw_power_brake_slowdown", 0x80))
+
+    def __init__(self, cuda_index, period=0.005):
+        self.period = period
+        self.samples = []
+        self.handle = None
+        self.max_mhz = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            uuid = getattr(torch.cuda.get_device_properties(cuda_index),
+                           "uuid", None)
+            try:
+                self.handle = pynvml.nvmlDeviceGetHandleByUUID(f"GPU-{uuid}")
+            except Exception:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(cuda_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(
+                self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.handle = None
+
+    def _sample(self):
+        n = self.nvml
+        sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+        try:
+            r = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+        except Exception:
+            r = n.nvmlDeviceGetCurrentClocksThrottleReasons(self.handle)
+        self.samples.append((sm, r))
+
+    def _loop(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            self._stop.wait(self.period)
 
     def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index),
-                 f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE,
-                stderr=subprocess.DEVNULL, text=True)
-        except Exception:
-            self.proc = None
+        import threading
+        if self.handle is None:
+            return
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._loop, daemon=True)
+        self._thread.start()
 
     def stop(self):
-        if self.proc is None:
+        if self.handle is None:
             return None
-        self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            self._sample()
         except Exception:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
-        sms, maxs, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
-                 "sw_power_cap"]
-        for line in out.strip().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 8:
-                continue
-            try:
-                sms.append(float(parts[0]))
-                maxs.append(float(parts[1]))
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[4:8]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not sms:
+            pass
+        self._stop.set()
+        self._thread.join()
+        if not self.samples:
             return None
-        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxs),
-                "samples": len(sms), "reasons": sorted(reasons)}
+        bits = 0
+        for _, r in self.samples:
+            bits |= int(r)
+        return {"sm_mhz": statistics.median(sm for sm, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "samples": len(self.samples),
+                "reasons": [name for name, b in self.REASONS if bits & b],
+                "source": "nvml"}
 
 
 # ---------------------------------------------------------------- traffic
@@ -169,78 +192,114 @@ def build_plan(cfg, torch):
     return plan
 
 
-def cpu_baseline(cfg, threads):
-    """Time the CPU oracle port of the reference algorithm on a bounded
-    sample and extrapolate to the full workload: pad + FFT once on the full
-    grid, interp/spread on a sample of the points, scaled by M / sample."""
-    from concurrent.futures import ThreadPoolExecutor
-    from oracle import port
-    x = cfg["x"]
-    M = x[0].size
-    dim = len(x)
-    if cfg["type"] == 2:
-        f = np.asarray(cfg["data"], dtype=np.complex128)
-        N = f.shape
-        w, beta, nup = port.fine_grid_sizes(N, cfg["eps"])
-        # plan-time work (excluded, as in the reference's exec protocol)
-        decs = []
-        for d in range(dim):
+class CpuPort:
+    """The CPU oracle port of the reference algorithm (oracle/port.py, fp64)
+    on the same type-2 workload: deconvolve + pad + FFT of the full grid,
+    then fold + interp of a sample of the points on `threads` threads.
+    Plan-time work (deconvolution factors) is done once in the constructor,
+    as the reference's exec protocol excludes it."""
+
+    def __init__(self, cfg, threads):
+        from oracle import port
+        if cfg["type"] != 2:
+            raise NotImplementedError("CPU baseline implemented for type-2 "
+                                      "configs")
+        self.port = port
+        self.cfg = cfg
+        self.threads = threads
+        self.x = cfg["x"]
+        self.M = self.x[0].size
+        self.dim = len(self.x)
+        self.f = np.asarray(cfg["data"], dtype=np.complex128)
+        N = self.f.shape
+        self.w, self.beta, self.nup = port.fine_grid_sizes(N, cfg["eps"])
+        self.decs = []
+        for d in range(self.dim):
             k = np.arange(-(N[d] // 2), N[d] - N[d] // 2, dtype=np.float64)
-            decs.append(1.0 / port.kernel_ft(2.0 * np.pi * k / nup[d], beta, w))
+            self.decs.append(1.0 / port.kernel_ft(2.0 * np.pi * k / self.nup[d],
+                                                  self.beta, self.w))
+
+    def step(self, sample):
+        """One pass: full grid work + interp of the first `sample` points.
+        Returns (grid seconds, point seconds)."""
+        from concurrent.futures import ThreadPoolExecutor
+        port, dim, N = self.port, self.dim, self.f.shape
         t0 = time.perf_counter()
-        g = f.copy()
+        g = self.f.copy()
         for d in range(dim):
-            g = g * decs[d].reshape((1,) * d + (-1,) + (1,) * (dim - d - 1))
-        H = np.zeros(nup, dtype=np.complex128)
-        H[np.ix_(*[port._band(N[d], nup[d]) for d in range(dim)])] = g
-        V = port._fft(H, cfg["isign"])
+            g = g * self.decs[d].reshape((1,) * d + (-1,) + (1,) * (dim - d - 1))
+        H = np.zeros(self.nup, dtype=np.complex128)
+        H[np.ix_(*[port._band(N[d], self.nup[d]) for d in range(dim)])] = g
+        V = port._fft(H, self.cfg["isign"])
         t_grid = time.perf_counter() - t0
-        sample = min(M, 2_000_000)
-        chunks = np.array_split(np.arange(sample), threads)
 
         def work(ix):
             i1s, frs = [], []
             for d in range(dim):
-                i1, fr64, _ = port.cells_fold(x[d][ix], nup[d], w)
+                i1, fr64, _ = port.cells_fold(self.x[d][ix], self.nup[d], self.w)
                 i1s.append(i1)
                 frs.append(fr64)
-            return port.interp(V, i1s, frs, w, beta, chunk=65536)
+            return port.interp(V, i1s, frs, self.w, self.beta, chunk=65536)
 
+        parts = [p for p in np.array_split(np.arange(sample), 4 * self.threads)
+                 if p.size]
         t1 = time.perf_counter()
-        with ThreadPoolExecutor(threads) as ex:
-            list(ex.map(work, chunks))
-        t_pts = time.perf_counter() - t1
-    else:
-        raise NotImplementedError("cpu baseline implemented for type-2 configs")
-    total = t_grid + t_pts * (M / sample)
-    return {"value": M / total, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": (f"oracle/port.py fp64: pad+FFT of the full grid "
-                       f"({t_grid:.2f} s) + interp of {sample} of {M} points "
-                       f"({t_pts:.2f} s), extrapolated to all points")}
+        with ThreadPoolExecutor(self.threads) as ex:
+            list(ex.map(work, parts))
+        return t_grid, time.perf_counter() - t1
+
+    def rate(self, t_grid, t_pts, sample):
+        """Points/s of the full workload from one step's times."""
+        return self.M / (t_grid + t_pts * (self.M / sample))
+
+    def describe(self, t_grid, t_pts, sample):
+        return (f"oracle/port.py fp64 on {self.threads} thread(s): "
+                f"deconvolve+pad+FFT of the full grid ({t_grid:.3f} s) + "
+                f"fold+interp of {sample} of {self.M} points ({t_pts:.3f} s)"
+                + ("" if sample == self.M else ", extrapolated to all points"))
 
 
-def run_reference(args):
-    """--impl reference: the CPU port, all host threads, rank 0 only."""
+def cpu_baseline(cfg, threads):
+    """One single-threaded pass of the CPU port over the whole workload."""
+    cp = CpuPort(cfg, threads)
+    sample = cp.M
+    tg, tp = cp.step(sample)
+    return {"value": cp.rate(tg, tp, sample), "unit": UNIT, "cores": threads,
+            "kind": "port", "sample": cp.describe(tg, tp, sample)}
+
+
+def run_reference(args, budget_s=150.0):
+    """--impl reference: the CPU port with all host threads, rank 0 only.
+    The first warm-up step calibrates the point rate; every step then
+    interpolates a sample sized so the whole run stays near `budget_s`."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from mlx_nufft_b200 import gen
     cfg = gen.config(args.config, scale=args.scale)
     threads = os.cpu_count() or 1
-    vals = []
+    cp = CpuPort(cfg, threads)
+    probe = min(cp.M, 200_000)
+    tg, tp = cp.step(probe)
+    per_step = budget_s / max(1, args.warmup + args.steps)
+    pts_rate = probe / max(tp, 1e-9)
+    sample = int(min(cp.M, max(20_000, (per_step - tg) * pts_rate)))
+    vals, last = [], None
     for i in range(args.warmup + args.steps):
-        r = cpu_baseline(cfg, threads)
+        tg, tp = cp.step(sample)
         if i >= args.warmup:
-            vals.append(r["value"])
+            vals.append(cp.rate(tg, tp, sample))
+            last = (tg, tp)
     v = float(np.median(vals))
-    r["value"] = v
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": cfg["x"][0].size / v * 1e3,
+            "ms_per_step": cp.M / v * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f64", "data": "synthetic",
             "config": {"workload": cfg["name"], "config": args.config},
-            "cpu_baseline": r,
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads,
+                             "kind": "port",
+                             "sample": cp.describe(*last, sample) + " (per step)"},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -300,13 +359,13 @@ def main():
         flush.zero_()
         step()
     barrier()
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.3)
     ev = [(torch.cuda.Event(enable_timing=True),
            torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     stage_ms = {"spread_or_pad": 0.0, "fft": 0.0, "interp_or_crop": 0.0}
+    sampler = ClockSampler(local)
+    launches0 = int(native.info().kernel_launches)
     barrier()
+    sampler.start()
     w0 = time.perf_counter()
     for i in range(args.steps):
         flush.zero_()
@@ -319,6 +378,7 @@ def main():
     barrier()
     wall = time.perf_counter() - w0
     clocks = sampler.stop()
+    launches = int(native.info().kernel_launches) - launches0
     native.set_profile(False)
     dev_ms = sum(a.elapsed_time(b) for a, b in ev)
     t = torch.tensor([dev_ms], dtype=torch.float64, device=dev)
@@ -328,22 +388,23 @@ def main():
     value = world * npts * args.steps / (tmax_ms / 1e3)
 
     # ---- e2e through the public API, pinned host buffers -----------------
+    # Each step: H2D copy of the step's input from pinned memory, execute,
+    # D2H copy of the result into a pinned host array, all inside the events.
     host_in = torch.from_numpy(np.ascontiguousarray(
         np.asarray(cfg["data"]).astype(np.complex64))).pin_memory()
+    host_out = torch.empty(n_out, dtype=torch.complex64).pin_memory()
     e2e_ms = []
-    for i in range(max(2, args.steps // 2) + 2):
+    n_e2e = max(3, min(args.steps, 30))
+    for i in range(n_e2e + 2):
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         flush.zero_()
         torch.cuda.synchronize()
         a.record()
-        if cfg["type"] == 2:
-            res = plan.execute(host_in, return_np=True)
-        elif cfg["type"] == 1:
-            res = plan.execute_batch(host_in.reshape(nvec, -1), return_np=True) \
-                if nvec > 1 else plan.execute(host_in, return_np=True)
+        if cfg["type"] == 1 and nvec > 1:
+            plan.execute_batch(host_in.reshape(nvec, -1), out=host_out)
         else:
-            res = plan.execute(host_in, return_np=True)
+            plan.execute(host_in, out=host_out)
         b.record()
         torch.cuda.synchronize()
         if i >= 2:
@@ -369,7 +430,6 @@ def main():
                 cpu = cpu_baseline(cfg, 1)
             except Exception as e:          # reported, never fatal
                 cpu = {"error": str(e)}
-        launches_per_step = 2 if cfg["type"] == 2 else (2 if cfg["type"] == 1 else 4)
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
@@ -393,8 +453,9 @@ def main():
             "e2e": {"value": e2e_val, "unit": UNIT,
                     "h2d_bytes_per_step": int(ndata * 8),
                     "d2h_bytes_per_step": int(n_out * 8),
-                    "ms_per_step": float(e2e_t.item())},
-            "gpu_launches": launches_per_step * args.steps,
+                    "ms_per_step": float(e2e_t.item()), "steps": n_e2e,
+                    "api": "plan.execute(pinned host in, out=pinned host)"},
+            "gpu_launches": launches,
             "clocks": clocks,
             "cpu_baseline": cpu,
         }

@@ -96,6 +96,8 @@ typedef struct nufft_plan_info {
     int     bin[3];                /* bin extent per dimension (tiled path)          */
     int64_t nsub, nsub_tgt;        /* subproblems (sources / type-3 targets)         */
     int64_t device_bytes;          /* device memory held by the plan                 */
+    int64_t kernel_launches;       /* this library's kernels launched by executes    */
+    int64_t fft_execs;             /* cuFFT executions issued by executes            */
 } nufft_plan_info;
 
 /* Fill `opts` with the defaults above. */

@@ -50,8 +50,28 @@ def numel(x):
     return int(np.asarray(x).size)
 
 
-def finish(t, return_np):
-    """Return a device tensor or its numpy copy."""
+def finish(t, return_np, out=None):
+    """Return a device tensor or its numpy copy; with `out` (a host numpy
+    array or a torch tensor of the result's size, e.g. pinned host memory),
+    copy the result into it and return `out`."""
+    if out is not None:
+        if isinstance(out, torch.Tensor):
+            if out.numel() != t.numel():
+                raise ValueError(f"out has {out.numel()} elements, result {t.numel()}")
+            out.view(-1).copy_(t.reshape(-1).to(out.dtype))
+            if out.device.type == "cpu":
+                torch.cuda.current_stream(t.device).synchronize()
+        else:
+            a = np.asarray(out)
+            if a.size != t.numel():
+                raise ValueError(f"out has {a.size} elements, result {t.numel()}")
+            host = torch.from_numpy(a.reshape(-1)) if a.dtype == np.complex64 \
+                else None
+            if host is not None and a.flags.c_contiguous:
+                host.copy_(t.reshape(-1))
+            else:
+                np.copyto(a, t.cpu().numpy().reshape(a.shape))
+        return out
     if return_np:
         return t.cpu().numpy()
     return t

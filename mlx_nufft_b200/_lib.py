@@ -65,6 +65,8 @@ class NufftPlanInfo(ctypes.Structure):
         ("nsub", ctypes.c_int64),
         ("nsub_tgt", ctypes.c_int64),
         ("device_bytes", ctypes.c_int64),
+        ("kernel_launches", ctypes.c_int64),
+        ("fft_execs", ctypes.c_int64),
     ]
 
 

@@ -28,7 +28,12 @@ void check_cuda(cudaError_t e, const char* what);
 void set_last_error(const std::string& msg);
 
 #define NUFFT_CUDA(call) ::nufft::check_cuda((call), #call)
-#define NUFFT_LAUNCH(what) ::nufft::check_cuda(cudaGetLastError(), what)
+// Every kernel launch in this library is followed by NUFFT_LAUNCH, which
+// checks the launch and counts it on the calling host thread (plans report
+// the launches of their executes from the difference of this count).
+inline thread_local int64_t launch_count = 0;
+#define NUFFT_LAUNCH(what) \
+    (++::nufft::launch_count, ::nufft::check_cuda(cudaGetLastError(), what))
 
 // ---------------------------------------------------------------------
 // host numerics (sizing.cpp) -- restatements of mlx_nufft/sizing.py

@@ -147,6 +147,8 @@ struct nufft_plan_s {
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     bool ev_recorded = false;
     int* d_err = nullptr;
+    int64_t launches = 0;      // own kernels launched by executes
+    int64_t fft_execs = 0;     // cuFFT executions issued by executes
 };
 
 namespace nufft_impl {
@@ -161,8 +163,12 @@ int env_int(const char* name, int dflt) {
 // ----------------------------------------------------------------------
 // tiling choice per grid: bin extent m per dimension so that the tile
 // (m + w - 1)^dim of complex64 fits shared memory with room for several
-// vectors.
-TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval) {
+// vectors.  1-D bins are 4096 cells for interpolation (each subproblem
+// loads its tile once, so longer bins cut the number of scattered output
+// windows) and 1024 for spreading (each subproblem flushes its whole tile);
+// 32 x 32 in 2-D, 8 x 8 x 8 in 3-D.
+TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
+                   bool interp) {
     TileGeom tg{};
     tg.dim = dim;
     tg.ncells = 1;
@@ -172,8 +178,9 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval) {
     tg.beta = (float)beta;
     tg.keval = keval ? 1 : 0;
     tg.poly = make_es_poly(w, beta);
-    static const int m1d = env_int("NUFFT_BIN_1D", 1024);
-    int m0 = dim == 1 ? m1d : (dim == 2 ? 32 : 8);
+    static const int m1d = env_int("NUFFT_BIN_1D", 0);
+    const int m1 = m1d > 0 ? m1d : (interp ? 4096 : 1024);
+    int m0 = dim == 1 ? m1 : (dim == 2 ? 32 : 8);
     for (int d = 0; d < 3; ++d) {
         if (d < dim) {
             tg.n[d] = (int)n[d];
@@ -277,6 +284,7 @@ void run_fft(nufft_plan_s* p, int nv, cudaStream_t st) {
     cufftHandle h = get_fft(p, nv);
     check_cufft(cufftSetStream(h, st), "cufftSetStream");
     const int dir = p->isign > 0 ? CUFFT_INVERSE : CUFFT_FORWARD;
+    ++p->fft_execs;
     if (p->fft64)
         check_cufft(cufftExecZ2Z(h, (cufftDoubleComplex*)p->gfft,
                                  (cufftDoubleComplex*)p->gfft, dir),
@@ -369,7 +377,8 @@ void create_t12(nufft_plan_s* p) {
         }
         upload_dec(p, d, v);
     }
-    p->tg_src = make_tile(p->dim, p->nup, p->w, p->beta, p->opts.kerevalmeth);
+    p->tg_src = make_tile(p->dim, p->nup, p->w, p->beta, p->opts.kerevalmeth,
+                          p->type == 2);
     p->nvg_src = vectors_per_tile(p->tg_src, p->nbatch);
     alloc_grids(p);
     p->sized = true;
@@ -471,9 +480,11 @@ void size_t3(nufft_plan_s* p, const double* slo, const double* shi) {
         destroy_ffts(p);
         alloc_grids(p);
     }
-    p->tg_src = make_tile(p->dim, p->nf, p->w, p->beta, p->opts.kerevalmeth);
+    p->tg_src = make_tile(p->dim, p->nf, p->w, p->beta, p->opts.kerevalmeth,
+                          false);
     p->nvg_src = vectors_per_tile(p->tg_src, p->nbatch);
-    p->tg_tgt = make_tile(p->dim, p->nup, p->w2, p->beta2, p->opts.kerevalmeth);
+    p->tg_tgt = make_tile(p->dim, p->nup, p->w2, p->beta2, p->opts.kerevalmeth,
+                          true);
     p->nvg_tgt = vectors_per_tile(p->tg_tgt, p->nbatch);
     p->sized = true;
 }
@@ -605,7 +616,9 @@ void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
                 record(p, 0, st);
                 record(p, 1, st);
             }
-            if (p->fft64) launch_widen(sg, (double2*)p->gfft, p->nupcells * nv, st);
+            if (p->fft64) {
+                launch_widen(sg, (double2*)p->gfft, p->nupcells * nv, st);
+                }
             run_fft(p, nv, st);
             record(p, 2, st);
             launch_crop(p->dim, p->N, p->nup, p->dec, p->gfft, p->fft64, out, nv,
@@ -827,6 +840,11 @@ int nufft_execute_stage(nufft_plan_t p, int stage, const void* in, void* out,
         const float2* fin = (const float2*)in;
         float2* fout = (float2*)out;
         const int64_t il = in_len(p), ol = out_len(p);
+        const int64_t l0 = launch_count;
+        struct Count {      // credited on every exit, exceptions included
+            nufft_plan_s* p; int64_t l0;
+            ~Count() { p->launches += launch_count - l0; }
+        } count{p, l0};
         for (int v0 = 0; v0 < nvec; v0 += p->nbatch) {
             const int nv = std::min(p->nbatch, nvec - v0);
             execute_chunk(p, fin ? fin + v0 * il : nullptr,
@@ -868,6 +886,7 @@ int nufft_execute_disjoint(nufft_plan_t p, const void* c, const int32_t* groups,
         // groups processed nbatch at a time; a group index outside the
         // current window is skipped by offsetting the labels on the fly.
         int32_t* shifted = (int32_t*)dmalloc(sizeof(int32_t) * p->src.M, "group labels");
+        const int64_t l0 = launch_count;
         try {
             for (int g0 = 0; g0 < ngroups; g0 += p->nbatch) {
                 const int ng = std::min(p->nbatch, ngroups - g0);
@@ -882,10 +901,12 @@ int nufft_execute_disjoint(nufft_plan_t p, const void* c, const int32_t* groups,
                             fo + (int64_t)g0 * p->K, ng, st);
             }
         } catch (...) {
+            p->launches += launch_count - l0;
             NUFFT_CUDA(cudaStreamSynchronize(st));
             dfree(shifted);
             throw;
         }
+        p->launches += launch_count - l0;
         NUFFT_CUDA(cudaStreamSynchronize(st));
         dfree(shifted);
     });
@@ -949,6 +970,8 @@ int nufft_plan_get_info(nufft_plan_t p, nufft_plan_info* info) {
         b += p->src.cap * (8 * p->dim + 4 + (p->src.phase ? 8 : 0));
         b += p->tgt.cap * (8 * p->dim + 4 + (p->tgt.phase ? 8 : 0));
         info->device_bytes = b;
+        info->kernel_launches = p->launches;
+        info->fft_execs = p->fft_execs;
     });
 }
 

@@ -159,14 +159,14 @@ class Type1PlanND(_PointsND):
         self._plan.execute(cs, out, nvec)
         return out
 
-    def execute(self, c, return_np=True):
+    def execute(self, c, return_np=True, out=None):
         if numel(c) != self.P:
             raise ValueError(f"c.size ({numel(c)}) must equal the number of "
                              f"nonuniform points ({self.P})")
         cs = as_c64(c, self._plan.device).reshape(-1)
-        return finish(self._run(cs, 1)[0], return_np)
+        return finish(self._run(cs, 1)[0], return_np, out)
 
-    def execute_batch(self, cs, return_np=True):
+    def execute_batch(self, cs, return_np=True, out=None):
         """B strength vectors over the same points through one shared spread
         (weights computed once per point) and one batched FFT; cs (B, P),
         returns (B, *N) (nd.py:744-794)."""
@@ -177,10 +177,10 @@ class Type1PlanND(_PointsND):
         t = as_c64(cs, self._plan.device)
         if B == 0:
             return finish(torch.empty((0,) + self.N, dtype=torch.complex64,
-                                      device=t.device), return_np)
-        return finish(self._run(t, B), return_np)
+                                      device=t.device), return_np, out)
+        return finish(self._run(t, B), return_np, out)
 
-    def execute_disjoint(self, c, groups, return_np=True):
+    def execute_disjoint(self, c, groups, return_np=True, out=None):
         """G disjoint subsets of the plan's points (groups[j] in [0, G)),
         each transformed independently; returns (G, *N) (nd.py:796-855)."""
         g = np.asarray(groups.cpu() if isinstance(groups, torch.Tensor)
@@ -192,14 +192,14 @@ class Type1PlanND(_PointsND):
                              f"nonuniform points ({self.P})")
         G = int(g.max()) + 1 if g.size else 0
         dev = self._plan.device
-        out = torch.zeros((G,) + self.N, dtype=torch.complex64,
+        res = torch.zeros((G,) + self.N, dtype=torch.complex64,
                           device=torch.device("cuda", dev))
         if G > 0:
             gt = torch.from_numpy(np.ascontiguousarray(g.astype(np.int32))).to(
-                out.device)
+                res.device)
             cs = as_c64(c, dev).reshape(-1)
-            self._plan.execute_disjoint(cs, gt, G, out)
-        return finish(out, return_np)
+            self._plan.execute_disjoint(cs, gt, G, res)
+        return finish(res, return_np, out)
 
 
 class Type2PlanND(_PointsND):
@@ -222,19 +222,19 @@ class Type2PlanND(_PointsND):
         self._plan.execute(fs, out, nvec)
         return out
 
-    def execute(self, fk, return_np=True):
+    def execute(self, fk, return_np=True, out=None):
         K = int(np.prod(self.N))
         if numel(fk) != K:
             raise ValueError(f"f.size ({numel(fk)}) must equal the mode-box "
                              f"size {tuple(self.N)}")
         fs = as_c64(fk, self._plan.device).reshape(-1)
-        return finish(self._run(fs, 1)[0], return_np)
+        return finish(self._run(fs, 1)[0], return_np, out)
 
-    def execute_batch(self, fks, return_np=True):
+    def execute_batch(self, fks, return_np=True, out=None):
         """B mode arrays (B, *N) -> (B, P) through one shared interp pass."""
         K = int(np.prod(self.N))
         t = as_c64(fks, self._plan.device)
         if t.numel() % K != 0:
             raise ValueError(f"fks must have shape (B, *{tuple(self.N)})")
         B = t.numel() // K
-        return finish(self._run(t.reshape(-1), B), return_np)
+        return finish(self._run(t.reshape(-1), B), return_np, out)

@@ -110,19 +110,19 @@ class Type3Plan:
         self._plan.execute(cs, out, nvec)
         return out
 
-    def execute(self, c, return_np=True):
+    def execute(self, c, return_np=True, out=None):
         assert numel(c) == self.P, \
             f"c.size ({numel(c)}) must equal number of sources ({self.P})"
         cs = as_c64(c, self._plan.device).reshape(-1)
-        return finish(self._run(cs, 1)[0], return_np)
+        return finish(self._run(cs, 1)[0], return_np, out)
 
-    def execute_batch(self, cs, return_np=True):
+    def execute_batch(self, cs, return_np=True, out=None):
         """(nch, P) strength channels -> (nch, M) through one batched pass."""
         t = as_c64(cs, self._plan.device)
         if t.dim() != 2:
             raise ValueError("cs must be 2-D (nch, P)")
         assert t.shape[1] == self.P
-        return finish(self._run(t.reshape(-1), int(t.shape[0])), return_np)
+        return finish(self._run(t.reshape(-1), int(t.shape[0])), return_np, out)
 
     def execute_profiled(self, c):
         """execute() with per-stage device times in seconds
