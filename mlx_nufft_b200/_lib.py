@@ -9,7 +9,9 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libnufft_b200.so")
+# NUFFT_B200_LIB names an alternate build of the same library (a tuning
+# build from `build.py --out PATH -DNAME=VALUE`); default: the in-tree one.
+LIB_PATH = os.environ.get("NUFFT_B200_LIB") or os.path.join(_HERE, "libnufft_b200.so")
 
 NUFFT_OK = 0
 NUFFT_ERR_ARG = -1

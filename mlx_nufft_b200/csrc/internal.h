@@ -100,6 +100,7 @@ struct TileGeom {
     int m[3];             // bin extent
     int nb[3];            // bins per dimension
     int T[3];             // tile extent m + w - 1 (unused dims 1)
+    uint32_t tdiv[3];     // ceil(2^32 / T[d]) for T[d] > 1 (division by T)
     int tcells;           // prod T
     int halfw;            // w / 2
     float c2w;            // (float)(2.0 / w)
@@ -148,10 +149,14 @@ struct PhaseParams {
     const double* fta;   // device: 128 weights a_q (post)
     int nq;
 };
+// cell_order: also order the points of each subproblem by cell (3-D
+// interpolation point sets only; measured slower for spreading, whose
+// shared atomics then collide, and for 1-D / 2-D interpolation, whose
+// scattered output stores lose their rough caller order).
 void build_pointset(PointSet* ps, const CellParams& cp, int64_t M,
                     const double* const* coords, bool sort, bool tiled,
-                    int msub, const PhaseParams& pp, int* d_err,
-                    cudaStream_t st);
+                    int msub, bool cell_order, const PhaseParams& pp,
+                    int* d_err, cudaStream_t st);
 void free_pointset(PointSet* ps);
 // min/max of `n` device arrays of length M each; out: 2*n doubles (min,max)
 void device_minmax(int n, const double* const* arrs, int64_t M, double* out,

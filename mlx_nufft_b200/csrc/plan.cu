@@ -194,6 +194,8 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
     for (int d = 0; d < dim; ++d) {
         tg.ncells *= n[d];
         tg.tcells *= tg.T[d];
+        tg.tdiv[d] = tg.T[d] > 1
+            ? (uint32_t)(((uint64_t)1 << 32) / (uint64_t)tg.T[d] + 1) : 0u;
     }
     return tg;
 }
@@ -403,7 +405,8 @@ void setpts_t12(nufft_plan_s* p, int64_t M, const double* const* xs,
     cp.chunk = tiled ? sort_chunk(p->dim) : 0;
     PhaseParams pp{};
     build_pointset(&p->src, cp, M, xs, sort, tiled,
-                   p->type == 1 ? kMsubSpread : kMsubInterp, pp, p->d_err, st);
+                   p->type == 1 ? kMsubSpread : kMsubInterp, p->type == 2, pp,
+                   p->d_err, st);
     check_err_flag(p, st);
     p->points_set = true;
 }
@@ -530,7 +533,8 @@ void set_sources_t3(nufft_plan_s* p, int64_t M, const double* const* xs,
     const bool tiled = want_tiled(p, M, p->tg_src);
     const bool sort = tiled || p->opts.sort_points;
     cp.chunk = tiled ? sort_chunk(p->dim) : 0;
-    build_pointset(&p->src, cp, M, xs, sort, tiled, kMsubSpread, pp, p->d_err, st);
+    build_pointset(&p->src, cp, M, xs, sort, tiled, kMsubSpread, false, pp,
+                   p->d_err, st);
     check_err_flag(p, st);
 }
 
@@ -591,7 +595,8 @@ void setpts_t3(nufft_plan_s* p, int64_t M, const double* const* xs, int64_t N,
     const bool tiled = want_tiled(p, N, p->tg_tgt);
     const bool sort = tiled || p->opts.sort_points;
     cp.chunk = tiled ? sort_chunk(p->dim) : 0;
-    build_pointset(&p->tgt, cp, N, ss, sort, tiled, kMsubInterp, pp, p->d_err, st);
+    build_pointset(&p->tgt, cp, N, ss, sort, tiled, kMsubInterp, true, pp,
+                   p->d_err, st);
     check_err_flag(p, st);
     p->Ntgt = N;
     // sources: guard against the extent only when it was given explicitly

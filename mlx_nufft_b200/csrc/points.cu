@@ -14,6 +14,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 
 #include "internal.h"
 
@@ -198,6 +199,82 @@ __global__ void k_sub_fill(const uint32_t* count, const uint32_t* start,
     }
 }
 
+// Order the points of every subproblem by their cell inside the bin
+// (row-major, last dimension fastest, the tile's memory order), so that a
+// warp's taps fall on neighbouring shared-memory words instead of random
+// banks.  One CTA per subproblem: shared histogram over the bin's cells
+// with per-point ranks, block-wide exclusive scan, scatter of cells and
+// permutation into the output arrays (same segment of the sorted order).
+// Shared memory: (cells per bin + msub) x 4 bytes.
+template <int DIM>
+__global__ void __launch_bounds__(256)
+k_sub_sort(const int4* __restrict__ subs, CellParams cp, int mcells,
+           const int2* __restrict__ i0, const int2* __restrict__ i1,
+           const int2* __restrict__ i2, const uint32_t* __restrict__ pin,
+           int2* __restrict__ o0, int2* __restrict__ o1, int2* __restrict__ o2,
+           uint32_t* __restrict__ pout) {
+    extern __shared__ uint32_t sm[];
+    uint32_t* hist = sm;              // mcells counters, then starts
+    uint32_t* slot = sm + mcells;     // per point: local cell | rank << 16
+    __shared__ uint32_t warp_tot[8];
+    const int4 sb = subs[blockIdx.x];
+    const int start = sb.x, cnt = sb.y;
+    int o[3] = {0, 0, 0};
+    {
+        int bin = sb.z;
+#pragma unroll
+        for (int d = DIM - 1; d >= 0; --d) {
+            o[d] = (bin % cp.nb[d]) * cp.m[d] - cp.halfw;
+            bin /= cp.nb[d];
+        }
+    }
+    const int2* in[3] = {i0, i1, i2};
+    for (int q = threadIdx.x; q < mcells; q += blockDim.x) hist[q] = 0u;
+    __syncthreads();
+    for (int t = threadIdx.x; t < cnt; t += blockDim.x) {
+        uint32_t loc = 0;
+#pragma unroll
+        for (int d = 0; d < DIM; ++d) {
+            int l = in[d][start + t].x - o[d];
+            l = min(max(l, 0), cp.m[d] - 1);   // setpts output is in range
+            loc = loc * (uint32_t)cp.m[d] + (uint32_t)l;
+        }
+        const uint32_t r = atomicAdd(hist + loc, 1u);
+        slot[t] = loc | (r << 16);
+    }
+    __syncthreads();
+    // exclusive scan of hist: each thread owns a contiguous run
+    const int per = (mcells + blockDim.x - 1) / blockDim.x;
+    const int b = threadIdx.x * per, e = min(mcells, b + per);
+    uint32_t run = 0;
+    for (int q = b; q < e; ++q) run += hist[q];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    uint32_t incl = run;
+#pragma unroll
+    for (int k = 1; k < 32; k <<= 1) {
+        const uint32_t v = __shfl_up_sync(0xffffffffu, incl, k);
+        if (lane >= k) incl += v;
+    }
+    if (lane == 31) warp_tot[wid] = incl;
+    __syncthreads();
+    uint32_t before = incl - run;
+    for (int w = 0; w < wid; ++w) before += warp_tot[w];
+    for (int q = b; q < e; ++q) {
+        const uint32_t v = hist[q];
+        hist[q] = before;
+        before += v;
+    }
+    __syncthreads();
+    int2* out[3] = {o0, o1, o2};
+    for (int t = threadIdx.x; t < cnt; t += blockDim.x) {
+        const uint32_t sl = slot[t];
+        const int pos = start + (int)(hist[sl & 0xffffu] + (sl >> 16));
+#pragma unroll
+        for (int d = 0; d < DIM; ++d) out[d][pos] = in[d][start + t];
+        pout[pos] = pin[start + t];
+    }
+}
+
 // Type-3 phases, written in sorted order (position j reads caller index
 // perm[j]).
 //  mode 1: prephase e^{i isign sum_d D_d x_d}            (gpu_t3.py:491-493)
@@ -326,10 +403,57 @@ void free_pointset(PointSet* ps) {
 
 namespace {
 
+// Cell order inside every subproblem (k_sub_sort) into fresh arrays, which
+// then replace the point set's cells and permutation.
+template <int DIM>
+void sub_sort(PointSet* ps, const CellParams& cp, int msub, cudaStream_t st) {
+    static const char* env = std::getenv("NUFFT_SUB_SORT");  // 0: off (tuning)
+    if (env && *env && std::atoi(env) == 0) return;
+    int mcells = 1;
+    for (int d = 0; d < DIM; ++d) mcells *= cp.m[d];
+    if (mcells > 65536 || msub > 65536) return;   // 16-bit slot fields
+    const size_t smem = sizeof(uint32_t) * ((size_t)mcells + (size_t)msub);
+    // opt in beyond the default dynamic limit (the kernel also has a few
+    // bytes of static shared memory)
+    if (smem > 40 * 1024) {
+        NUFFT_CUDA(cudaFuncSetAttribute((const void*)k_sub_sort<DIM>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)smem));
+    }
+    int2* nc[3] = {nullptr, nullptr, nullptr};
+    uint32_t* np = nullptr;
+    try {
+        for (int d = 0; d < DIM; ++d)
+            nc[d] = (int2*)dmalloc(sizeof(int2) * ps->cap, "sorted cells");
+        np = (uint32_t*)dmalloc(4 * ps->cap, "sorted permutation");
+    } catch (...) {
+        for (int d = 0; d < DIM; ++d) dfree(nc[d]);
+        throw;
+    }
+    try {
+        k_sub_sort<DIM><<<(unsigned)ps->nsub, 256, smem, st>>>(
+            ps->subs, cp, mcells, ps->cell[0], ps->cell[1], ps->cell[2],
+            ps->perm, nc[0], nc[1], nc[2], np);
+        NUFFT_LAUNCH("k_sub_sort");
+        NUFFT_CUDA(cudaStreamSynchronize(st));
+    } catch (...) {
+        for (int d = 0; d < DIM; ++d) dfree(nc[d]);
+        dfree(np);
+        throw;
+    }
+    for (int d = 0; d < DIM; ++d) {
+        dfree(ps->cell[d]);
+        ps->cell[d] = nc[d];
+    }
+    dfree(ps->perm);
+    ps->perm = np;
+}
+
 template <int DIM>
 void build_impl(PointSet* ps, const CellParams& cp, int64_t M,
                 const double* const* coords, bool sort, bool tiled, int msub,
-                const PhaseParams& pp, int* d_err, cudaStream_t st) {
+                bool cell_order, const PhaseParams& pp, int* d_err,
+                cudaStream_t st) {
     Coords X{};
     for (int d = 0; d < DIM; ++d) X.p[d] = coords[d];
     const int bs = 256;
@@ -386,6 +510,8 @@ void build_impl(PointSet* ps, const CellParams& cp, int64_t M,
             NUFFT_CUDA(cudaStreamSynchronize(st));
             dfree(nsubs);
             dfree(subofs);
+            if (h_tot > 0 && cell_order && DIM == 3)
+                sub_sort<DIM>(ps, cp, msub, st);
         }
         NUFFT_CUDA(cudaStreamSynchronize(st));
         dfree(key_of);
@@ -405,8 +531,8 @@ void build_impl(PointSet* ps, const CellParams& cp, int64_t M,
 
 void build_pointset(PointSet* ps, const CellParams& cp, int64_t M,
                     const double* const* coords, bool sort, bool tiled,
-                    int msub, const PhaseParams& pp, int* d_err,
-                    cudaStream_t st) {
+                    int msub, bool cell_order, const PhaseParams& pp,
+                    int* d_err, cudaStream_t st) {
     if (M < 1) fail(-1, "at least one nonuniform point is required");
     if (M >= (int64_t)0x7fffffffLL)
         fail(-1, "at most 2^31-1 nonuniform points per plan");
@@ -425,9 +551,9 @@ void build_pointset(PointSet* ps, const CellParams& cp, int64_t M,
     ps->sorted = sort;
     ps->tiled = tiled && sort;
     switch (cp.dim) {
-        case 1: build_impl<1>(ps, cp, M, coords, sort, tiled, msub, pp, d_err, st); break;
-        case 2: build_impl<2>(ps, cp, M, coords, sort, tiled, msub, pp, d_err, st); break;
-        case 3: build_impl<3>(ps, cp, M, coords, sort, tiled, msub, pp, d_err, st); break;
+        case 1: build_impl<1>(ps, cp, M, coords, sort, tiled, msub, cell_order, pp, d_err, st); break;
+        case 2: build_impl<2>(ps, cp, M, coords, sort, tiled, msub, cell_order, pp, d_err, st); break;
+        case 3: build_impl<3>(ps, cp, M, coords, sort, tiled, msub, cell_order, pp, d_err, st); break;
         default: fail(-1, "dim must be 1, 2 or 3");
     }
 }

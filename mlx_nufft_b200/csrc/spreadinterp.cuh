@@ -42,19 +42,35 @@ __device__ __forceinline__ float es_weight(float d, float c2w, float beta) {
     return expf(beta * (sqrtf(t) - 1.0f));
 }
 
-// All W weights psi(l - fr), l = 0..W-1, by Horner evaluation of the
-// plan's per-tap polynomials in t = fr - (W/2 - 1/2).
+// All W weights psi(l - fr), l = 0..W-1, from the plan's per-tap
+// polynomials p_l(t), t = fr - (W/2 - 1/2).  The ES kernel is even, so
+// p_{W-1-l}(t) = p_l(-t): splitting p_l(t) = E_l(t^2) + t O_l(t^2) gives
+// both mirrored taps from one Horner pass each over the even and the odd
+// coefficients (about half the FMAs of W separate evaluations).  The
+// middle tap of an odd width is even in t and uses E alone.
 template <int W>
 __device__ __forceinline__ void es_weights(float fr, const EsPoly& P,
                                            float* wt) {
     constexpr int D = es_degree(W);
+    constexpr int KE = D - (D & 1);          // highest even power
+    constexpr int KO = D - 1 + (D & 1);      // highest odd power
     const float t = fr - (0.5f * W - 0.5f);
+    const float u = t * t;
 #pragma unroll
-    for (int l = 0; l < W; ++l) wt[l] = P.c[D][l];
+    for (int l = 0; l < (W + 1) / 2; ++l) {
+        float e = P.c[KE][l];
 #pragma unroll
-    for (int k = D - 1; k >= 0; --k)
+        for (int k = KE - 2; k >= 0; k -= 2) e = fmaf(e, u, P.c[k][l]);
+        if (2 * l + 1 == W) {
+            wt[l] = e;
+        } else {
+            float o = P.c[KO][l];
 #pragma unroll
-        for (int l = 0; l < W; ++l) wt[l] = fmaf(wt[l], t, P.c[k][l]);
+            for (int k = KO - 2; k >= 1; k -= 2) o = fmaf(o, u, P.c[k][l]);
+            wt[l] = fmaf(t, o, e);
+            wt[W - 1 - l] = fmaf(-t, o, e);
+        }
+    }
 }
 
 // Weights by the plan's evaluation method: per-tap polynomials (keval 1)
@@ -131,21 +147,34 @@ __device__ __forceinline__ void bin_origin(int bin, const TileGeom& tg,
     }
 }
 
-// Global linear cell of tile index q, with periodic wrap.
+// Periodic wrap of a tile coordinate: one compare in the common case
+// (tile cells lie within one period of [0, n)), remainder otherwise.
+__device__ __forceinline__ int wrap_tile(int x, int n) {
+    return ((unsigned)x < (unsigned)n) ? x : wrapmod(x, n);
+}
+
+// Global linear cell of tile index q (row-major over T, last dimension
+// fastest), with periodic wrap.  q / T[d] by multiply-high with the
+// plan's reciprocal tdiv[d] = ceil(2^32 / T[d]) (exact for q T[d] < 2^32).
 template <int DIM>
 __device__ __forceinline__ int64_t tile_to_global(int q, const int* o,
                                                   const TileGeom& tg) {
-    int p[3];
-#pragma unroll
-    for (int d = DIM - 1; d >= 0; --d) {
-        p[d] = q % tg.T[d];
-        q /= tg.T[d];
+    if constexpr (DIM == 1) {
+        return wrap_tile(o[0] + q, tg.n[0]);
+    } else if constexpr (DIM == 2) {
+        const int r = (int)__umulhi((unsigned)q, tg.tdiv[1]);
+        const int x = q - r * tg.T[1];
+        return (int64_t)wrap_tile(o[0] + r, tg.n[0]) * tg.n[1] +
+               wrap_tile(o[1] + x, tg.n[1]);
+    } else {
+        const int r = (int)__umulhi((unsigned)q, tg.tdiv[2]);
+        const int x = q - r * tg.T[2];
+        const int z = (int)__umulhi((unsigned)r, tg.tdiv[1]);
+        const int y = r - z * tg.T[1];
+        return ((int64_t)wrap_tile(o[0] + z, tg.n[0]) * tg.n[1] +
+                wrap_tile(o[1] + y, tg.n[1])) * tg.n[2] +
+               wrap_tile(o[2] + x, tg.n[2]);
     }
-    int64_t g = 0;
-#pragma unroll
-    for (int d = 0; d < DIM; ++d)
-        g = g * tg.n[d] + wrapmod(o[d] + p[d], tg.n[d]);
-    return g;
 }
 
 // ES weights of one point in every dimension; returns false if the point's
@@ -294,8 +323,20 @@ __device__ __forceinline__ void scheduler_done(int* sched) {
 // loads of a whole batch (cells, permutation, phase: streamed once, so
 // cache-streaming hints) are issued before any of its math, keeping U
 // independent DRAM requests in flight per thread.
+#ifndef NUFFT_U_1D
+#define NUFFT_U_1D 4
+#endif
 template <int DIM>
-__host__ __device__ constexpr int batch_u() { return DIM == 3 ? 2 : 4; }
+__host__ __device__ constexpr int batch_u() {
+    return DIM == 3 ? 2 : (DIM == 1 ? NUFFT_U_1D : 4);
+}
+
+// Resident CTAs per SM the tiled interpolation is compiled for: caps its
+// registers at 64 so four 256-thread CTAs fit an SM (its tile needs at
+// most a quarter of the shared memory).
+#ifndef NUFFT_INTERP_MINB
+#define NUFFT_INTERP_MINB 4
+#endif
 
 // --------------------------------------------------------------------
 // tiled spread: grid[v] += sum_j c[v][perm j] * phase_j * psi-tensor
@@ -371,7 +412,7 @@ k_spread_tiled(const float2* __restrict__ c, int64_t cstride, int nvg,
 // --------------------------------------------------------------------
 // tiled interp: out[v][perm j] = phase_j * sum taps tile[v] * psi-tensor
 template <int DIM, int W, typename G>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, NUFFT_INTERP_MINB)
 k_interp_tiled(const G* __restrict__ grid, int nvg,
                const uint32_t* __restrict__ perm, CellPtrs cells,
                const float2* __restrict__ phase, const int4* __restrict__ subs,

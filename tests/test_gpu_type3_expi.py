@@ -134,12 +134,22 @@ def test_type3_batch_equals_loop(rng):
     s = [rng.uniform(-7, 7, 25_000) for _ in range(3)]
     cs = (rng.standard_normal((3, 30_000)) +
           1j * rng.standard_normal((3, 30_000))).astype(np.complex64)
-    plan = Type3Plan(tuple(x), tuple(s), eps=1e-5)
+    eps = 1e-5
+    plan = Type3Plan(tuple(x), tuple(s), eps=eps)
     fb = plan.execute_batch(cs)
+    idx = rng.choice(25_000, 2000, replace=False)
     for b in range(3):
-        # equal up to run-to-run atomic-order noise, amplified by 1/phihat
-        # at sigma = 1.25 (the reference's note, gpu_t3.py:944-946)
-        assert port.rel_l2(fb[b], plan.execute(cs[b])) < 1e-4
+        single = plan.execute(cs[b])
+        exact = fast.direct_sum(x, cs[b], s, +1, idx)
+        ref32 = port.nufft_t3_fp32(x, cs[b], s, eps=eps, isign=+1)
+        bound = max(gate(eps), REF32_SLACK * port.rel_l2(ref32[idx], exact))
+        # each channel of the batch, and the separate execute, meet the
+        # accuracy gate; they differ from each other only by the
+        # run-to-run atomic-order noise that 1/phihat amplifies at
+        # sigma = 1.25 (gpu_t3.py:944-947)
+        assert port.rel_l2(fb[b][idx], exact) <= bound
+        assert port.rel_l2(single[idx], exact) <= bound
+        assert port.rel_l2(fb[b], single) <= 2 * bound
 
 
 # ---------------------------------------------------------------- expi
