@@ -59,8 +59,10 @@ extern "C" {
 
 /* ---- execute stages (nufft_execute_stage) ---------------------------- */
 #define NUFFT_STAGE_ALL     0   /* whole transform == nufft_execute            */
-#define NUFFT_STAGE_SPREAD  1   /* type 1: zero the fine grid(s) and spread    */
-#define NUFFT_STAGE_FINISH  2   /* type 1: FFT + deconvolve/crop of the grid(s) */
+#define NUFFT_STAGE_SPREAD  1   /* type 1: zero the fine grid(s) and spread;   */
+                                /* type 2: pad/deconvolve the modes + FFT      */
+#define NUFFT_STAGE_FINISH  2   /* type 1: FFT + deconvolve/crop of the grid(s);*/
+                                /* type 2: interpolate from the fine grid(s)    */
 
 typedef struct nufft_plan_s* nufft_plan_t;
 
@@ -98,6 +100,7 @@ typedef struct nufft_plan_info {
     int64_t device_bytes;          /* device memory held by the plan                 */
     int64_t kernel_launches;       /* this library's kernels launched by executes    */
     int64_t fft_execs;             /* cuFFT executions issued by executes            */
+    int     fft64;                 /* 1 if the fine-grid FFT runs in fp64            */
 } nufft_plan_info;
 
 /* Fill `opts` with the defaults above. */
@@ -145,15 +148,20 @@ int nufft_set_sources(nufft_plan_t plan, int64_t M, const double* x,
 int nufft_execute(nufft_plan_t plan, const void* in, void* out, int nvec,
                   void* stream);
 
-/* Type 1 only: one stage of nufft_execute on nvec <= n_trans vectors, so a
- * caller can reduce the fine grids across GPUs between SPREAD and FINISH.
- * SPREAD reads `in`, FINISH writes `out`.  No reference counterpart (the
- * reference is single-GPU); it splits Type1PlanND.execute (nd.py:581-625). */
+/* Types 1 and 2: one stage of nufft_execute on nvec <= n_trans vectors, so
+ * a caller can combine the fine grids across GPUs between the stages: sum
+ * type-1 grids of ranks that spread disjoint points, or broadcast one
+ * type-2 grid to ranks that interpolate disjoint targets.  SPREAD reads
+ * `in`, FINISH writes `out`.  No reference counterpart (the reference is
+ * single-GPU); it splits Type1PlanND.execute (nd.py:581-625) and
+ * Type2PlanND.execute (nd.py:1075-1119). */
 int nufft_execute_stage(nufft_plan_t plan, int stage, const void* in,
                         void* out, int nvec, void* stream);
 
-/* Device address and size (complex64 elements, all n_trans grids) of the
- * plan's fine grid, e.g. for a collective between the stages above.        */
+/* Device address and size (elements, all n_trans grids) of the plan's fine
+ * grid, e.g. for a collective between the stages above: type 1 the
+ * complex64 spreading grid; type 2 the FFT grid, complex128 when the plan
+ * runs its FFT in fp64 (nufft_plan_info.fft64), else complex64.            */
 int nufft_get_grid(nufft_plan_t plan, void** grid, int64_t* n_complex);
 
 /* Type 1 only: transform G disjoint subsets of the plan's points

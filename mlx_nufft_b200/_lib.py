@@ -24,7 +24,7 @@ NUFFT_ERR_UNSUPPORTED = -7
 
 PREC = {"crit64": 0, "fp32": 1, "coords64": 2, "phases64": 3}
 METHOD = {"auto": 0, "od": 1, "tiled": 1, "gm": 2, "global": 2}
-STAGE_ALL, STAGE_SPREAD, STAGE_FINISH = 0, 1, 2
+STAGE_ALL, STAGE_SPREAD, STAGE_FINISH = 0, 1, 2   # type 2: grid, interp
 
 c_double_p = ctypes.POINTER(ctypes.c_double)
 c_int64_p = ctypes.POINTER(ctypes.c_int64)
@@ -69,6 +69,7 @@ class NufftPlanInfo(ctypes.Structure):
         ("device_bytes", ctypes.c_int64),
         ("kernel_launches", ctypes.c_int64),
         ("fft_execs", ctypes.c_int64),
+        ("fft64", ctypes.c_int),
     ]
 
 

@@ -127,7 +127,8 @@ struct PointSet {
 
 // CTAs for a persistent launch of `kernel` (256 threads, `smem` bytes):
 // resident CTAs per SM x SMs, capped at `work` items.
-int persistent_grid(const void* kernel, size_t smem, int64_t work);
+int persistent_grid(const void* kernel, size_t smem, int64_t work,
+                    int threads = 256);
 
 // ---------------------------------------------------------------------
 // device memory helpers

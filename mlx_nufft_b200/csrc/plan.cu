@@ -154,7 +154,7 @@ struct nufft_plan_s {
 namespace nufft_impl {
 
 // Integer tuning override from the environment (NUFFT_BIN_1D,
-// NUFFT_SORT_CHUNK_LOG2); the default when unset.
+// NUFFT_SORT_CHUNK_LOG2, NUFFT_TILE_KB); the default when unset.
 int env_int(const char* name, int dflt) {
     const char* v = std::getenv(name);
     return (v && *v) ? std::atoi(v) : dflt;
@@ -222,7 +222,9 @@ bool tile_fits(const TileGeom& tg) {
 
 int vectors_per_tile(const TileGeom& tg, int nbatch) {
     const size_t per = (size_t)tg.tcells * sizeof(float2);
-    int nvg = (int)std::max<size_t>(1, kTileBudget / per);
+    static const int kb = env_int("NUFFT_TILE_KB", 0);   // tuning override
+    const size_t budget = kb > 0 ? (size_t)kb * 1024 : kTileBudget;
+    int nvg = (int)std::max<size_t>(1, budget / per);
     if ((size_t)nvg * per > tile_bytes_max())
         nvg = (int)std::max<size_t>(1, tile_bytes_max() / per);
     return std::max(1, std::min(nvg, nbatch));
@@ -631,11 +633,23 @@ void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
             record(p, 3, st);
         }
     } else if (p->type == 2) {
-        record(p, 0, st);
-        launch_pad(p->dim, p->N, p->nup, p->dec, in, p->gfft, p->fft64, nv, st);
-        record(p, 1, st);
-        run_fft(p, nv, st);
-        record(p, 2, st);
+        if (stage == NUFFT_STAGE_ALL || stage == NUFFT_STAGE_SPREAD) {
+            record(p, 0, st);
+            launch_pad(p->dim, p->N, p->nup, p->dec, in, p->gfft, p->fft64, nv, st);
+            record(p, 1, st);
+            run_fft(p, nv, st);
+            record(p, 2, st);
+        }
+        if (stage == NUFFT_STAGE_SPREAD) {
+            record(p, 3, st);
+            p->ev_recorded = p->profile;
+            return;
+        }
+        if (stage == NUFFT_STAGE_FINISH) {
+            record(p, 0, st);
+            record(p, 1, st);
+            record(p, 2, st);
+        }
         launch_interp(p->src, p->tg_src, p->w, p->gfft, p->fft64, nv, out,
                       p->src.M, p->nvg_src, st);
         record(p, 3, st);
@@ -830,7 +844,7 @@ int nufft_execute_stage(nufft_plan_t p, int stage, const void* in, void* out,
         if (!p->points_set) fail(NUFFT_ERR_STATE, "setpts() must be called before execute()");
         if (nvec < 1) fail(NUFFT_ERR_ARG, "nvec must be >= 1");
         if (stage != NUFFT_STAGE_ALL) {
-            if (p->type != 1) fail(NUFFT_ERR_ARG, "stages apply to type-1 plans only");
+            if (p->type == 3) fail(NUFFT_ERR_ARG, "stages apply to type-1 and type-2 plans");
             if (nvec > p->nbatch) fail(NUFFT_ERR_ARG, "staged execute: nvec exceeds the plan batch");
             if (stage != NUFFT_STAGE_SPREAD && stage != NUFFT_STAGE_FINISH)
                 fail(NUFFT_ERR_ARG, "unknown stage");
@@ -977,6 +991,7 @@ int nufft_plan_get_info(nufft_plan_t p, nufft_plan_info* info) {
         info->device_bytes = b;
         info->kernel_launches = p->launches;
         info->fft_execs = p->fft_execs;
+        info->fft64 = p->fft64 ? 1 : 0;
     });
 }
 

@@ -1,5 +1,6 @@
 // spread.cu -- launchers for the spreading kernels (types 1 and 3).
 #include <algorithm>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <set>
@@ -21,7 +22,7 @@ int tile_smem_limit() {
     return limit;
 }
 
-int persistent_grid(const void* kernel, size_t smem, int64_t work) {
+int persistent_grid(const void* kernel, size_t smem, int64_t work, int threads) {
     static std::mutex mu;
     static std::map<std::pair<const void*, size_t>, int> cache;
     static int sms = 0;
@@ -33,13 +34,13 @@ int persistent_grid(const void* kernel, size_t smem, int64_t work) {
             NUFFT_CUDA(cudaGetDevice(&dev));
             NUFFT_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
         }
-        auto key = std::make_pair(kernel, smem);
+        auto key = std::make_pair(kernel, smem * 4096 + (size_t)threads);
         auto it = cache.find(key);
         if (it != cache.end()) {
             per_sm = it->second;
         } else {
             NUFFT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel,
-                                                                     256, smem));
+                                                                     threads, smem));
             per_sm = std::max(per_sm, 1);
             cache[key] = per_sm;
         }
@@ -66,6 +67,24 @@ void ensure_smem(const void* kernel, size_t bytes) {
 
 namespace {
 
+constexpr size_t kPlaneTileBudget = 96 * 1024;
+
+// 3-D plane-owned spreading of NV vectors per launch.
+template <int W, int NV>
+void launch_planes(const PointSet& ps, const TileGeom& tg, const float2* c,
+                   int64_t cstride, const uint32_t* perm, const CellPtrs& cells,
+                   float2* grid, cudaStream_t st) {
+    auto k = k_spread_planes<W, NV>;
+    const size_t smem = (size_t)NV * tg.tcells * sizeof(float2);
+    ensure_smem((const void*)k, smem);
+    const int blocks = persistent_grid((const void*)k, smem, ps.nsub,
+                                       32 * kPlaneWarps);
+    k<<<blocks, 32 * kPlaneWarps, smem, st>>>(c, cstride, perm, cells, ps.phase,
+                                               ps.subs, (int)ps.nsub, ps.sched,
+                                               grid, tg);
+    NUFFT_LAUNCH("k_spread_planes");
+}
+
 template <int DIM, int W>
 void spread_impl(const PointSet& ps, const TileGeom& tg, const float2* c,
                  int64_t cstride, int nvec, float2* grid, int nvg,
@@ -74,6 +93,22 @@ void spread_impl(const PointSet& ps, const TileGeom& tg, const float2* c,
     const CellPtrs cells = cell_ptrs(ps);
     if (ps.tiled) {
         if (ps.nsub == 0) return;
+        if constexpr (DIM == 3 && W <= 10) {
+            // groups of 4, 2 or 1 vectors, each group's tile within 96 KB
+            const size_t per = (size_t)tg.tcells * sizeof(float2);
+            for (int v0 = 0; v0 < nvec;) {
+                const int left = nvec - v0;
+                const int nv = (left >= 4 && 4 * per <= kPlaneTileBudget) ? 4
+                             : (left >= 2 && 2 * per <= kPlaneTileBudget) ? 2 : 1;
+                const float2* cv = c + v0 * cstride;
+                float2* gv = grid + v0 * tg.ncells;
+                if (nv == 4) launch_planes<W, 4>(ps, tg, cv, cstride, perm, cells, gv, st);
+                else if (nv == 2) launch_planes<W, 2>(ps, tg, cv, cstride, perm, cells, gv, st);
+                else launch_planes<W, 1>(ps, tg, cv, cstride, perm, cells, gv, st);
+                v0 += nv;
+            }
+            return;
+        }
         auto k = k_spread_tiled<DIM, W>;
         for (int v0 = 0; v0 < nvec; v0 += nvg) {
             const int nv = std::min(nvg, nvec - v0);

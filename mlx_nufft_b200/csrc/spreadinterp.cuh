@@ -331,6 +331,147 @@ __host__ __device__ constexpr int batch_u() {
     return DIM == 3 ? 2 : (DIM == 1 ? NUFFT_U_1D : 4);
 }
 
+// --------------------------------------------------------------------
+// tiled spread, 3-D: plane-owned shared tile, no shared-memory atomics.
+//
+// Float atomicAdd on shared memory is a load / compare-and-swap loop on this
+// GPU (8 conflict-free lane-ops per clock per SM, far fewer when a CTA's
+// warps update one small tile).  Here warp k of the CTA owns the tile
+// planes z (dimension 0) with z mod 8 == k, and only warp k ever writes
+// them, so a plain shared load / FMA / store cannot race: a point touches
+// W <= 8 consecutive planes, i.e. at most one plane per warp (W > 8: at
+// most two), and within a plane the lanes take distinct (y, x) taps.
+// __syncwarp() orders one point's stores before the next point's loads.
+//
+// Points are staged 128 at a time: one thread per point computes its tile
+// offset, its 3 x W kernel weights and its NV strengths (times the phase)
+// into shared memory; then every warp walks the staged points and updates
+// its plane of each.  The flush adds the tile to the fine grid with one
+// float2 global atomic per touched cell.
+constexpr int kPlaneWarps = 8;
+constexpr int kPlaneChunk = 128;
+
+template <int W, int NV>
+__global__ void __launch_bounds__(32 * kPlaneWarps)
+k_spread_planes(const float2* __restrict__ c, int64_t cstride,
+                const uint32_t* __restrict__ perm, CellPtrs cells,
+                const float2* __restrict__ phase, const int4* __restrict__ subs,
+                int nsub, int* __restrict__ sched, float2* __restrict__ grid,
+                TileGeom tg) {
+    constexpr int W2 = W * W;
+    constexpr int NR = (W2 + 31) / 32;               // rounds per plane
+    extern __shared__ float2 tile[];                 // [NV][T]
+    __shared__ int s_l0[kPlaneChunk];                // l0z, tile offset of (l0z, l0y, l0x)
+    __shared__ int s_off[kPlaneChunk];
+    __shared__ float s_w[kPlaneChunk][3 * W];
+    __shared__ float2 s_c[kPlaneChunk][NV];
+    __shared__ int s_sub;
+    const int T = tg.tcells;
+    const int T2 = tg.T[2], TT = tg.T[1] * tg.T[2];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    // this lane's (y, x) tap in each round and its offset inside a plane
+    int rb[NR], rk[NR], roff[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+        const int t = min(r * 32 + lane, W2 - 1);
+        rb[r] = t / W;
+        rk[r] = t - rb[r] * W;
+        roff[r] = rb[r] * T2 + rk[r];
+    }
+    for (;;) {
+        const int sub = next_subproblem(sched, &s_sub);    // (syncs)
+        if (sub >= nsub) break;
+        const int4 sb = subs[sub];
+        const int start = sb.x, cnt = sb.y;
+        int o[3] = {0, 0, 0};
+        bin_origin<3>(sb.z, tg, o);
+        for (int q = threadIdx.x; q < NV * T; q += blockDim.x)
+            tile[q] = make_float2(0.0f, 0.0f);
+        for (int c0 = 0; c0 < cnt; c0 += kPlaneChunk) {
+            const int n = min(kPlaneChunk, cnt - c0);
+            __syncthreads();      // tile zeroed / previous chunk consumed
+            if (threadIdx.x < n) {
+                const int p = threadIdx.x;
+                const int64_t j = start + c0 + p;
+                int l0[3];
+                bool ok = true;
+#pragma unroll
+                for (int d = 0; d < 3; ++d) {
+                    const int2 cl = __ldg(cells.d[d] + j);
+                    l0[d] = cl.x - o[d];
+                    ok &= (unsigned)l0[d] < (unsigned)tg.m[d];
+                    float wt[W];
+                    kernel_weights<W>(__int_as_float(cl.y), tg, wt);
+#pragma unroll
+                    for (int l = 0; l < W; ++l) s_w[p][d * W + l] = wt[l];
+                }
+                // l0z = -1 marks a point outside the bin (never for
+                // consistent setpts output): every warp skips it
+                s_l0[p] = ok ? l0[0] : -1;
+                s_off[p] = l0[1] * T2 + l0[2];
+                const int64_t src = perm ? (int64_t)__ldg(perm + j) : j;
+                const float2 ph = phase ? __ldg(phase + j) : make_float2(1.0f, 0.0f);
+#pragma unroll
+                for (int v = 0; v < NV; ++v) {
+                    float2 cv = __ldg(c + v * cstride + src);
+                    if (phase) cv = cmul(cv, ph);
+                    s_c[p][v] = cv;
+                }
+            }
+            __syncthreads();
+            for (int p = 0; p < n; ++p) {
+                const int l0z = s_l0[p];
+                if (l0z < 0) continue;
+                // planes z = l0z + a owned by this warp: a = (wid - l0z) mod 8
+                for (int a = (wid - l0z) & (kPlaneWarps - 1); a < W; a += kPlaneWarps) {
+                    const float wa = s_w[p][a];
+                    const int base = (l0z + a) * TT + s_off[p];
+                    float2 cv[NV];
+#pragma unroll
+                    for (int v = 0; v < NV; ++v) {
+                        const float2 cc = s_c[p][v];
+                        cv[v] = make_float2(cc.x * wa, cc.y * wa);
+                    }
+                    float wr[NR];
+                    int q[NR];
+#pragma unroll
+                    for (int r = 0; r < NR; ++r) {
+                        wr[r] = s_w[p][W + rb[r]] * s_w[p][2 * W + rk[r]];
+                        q[r] = base + roff[r];
+                    }
+                    float2 g[NR][NV];
+#pragma unroll
+                    for (int r = 0; r < NR; ++r)
+                        if (r * 32 + lane < W2)
+#pragma unroll
+                            for (int v = 0; v < NV; ++v) g[r][v] = tile[v * T + q[r]];
+#pragma unroll
+                    for (int r = 0; r < NR; ++r)
+                        if (r * 32 + lane < W2)
+#pragma unroll
+                            for (int v = 0; v < NV; ++v) {
+                                g[r][v].x = fmaf(cv[v].x, wr[r], g[r][v].x);
+                                g[r][v].y = fmaf(cv[v].y, wr[r], g[r][v].y);
+                                tile[v * T + q[r]] = g[r][v];
+                            }
+                }
+                __syncwarp();
+            }
+        }
+        __syncthreads();
+        for (int q = threadIdx.x; q < T; q += blockDim.x) {
+            const int64_t g = tile_to_global<3>(q, o, tg);
+#pragma unroll
+            for (int v = 0; v < NV; ++v) {
+                const float2 val = tile[v * T + q];
+                if (val.x != 0.0f || val.y != 0.0f)
+                    atomicAdd(grid + v * tg.ncells + g, val);
+            }
+        }
+    }
+    scheduler_done(sched);
+}
+
 // Resident CTAs per SM the tiled interpolation is compiled for: caps its
 // registers at 64 so four 256-thread CTAs fit an SM (its tile needs at
 // most a quarter of the shared memory).
@@ -339,7 +480,10 @@ __host__ __device__ constexpr int batch_u() {
 #endif
 
 // --------------------------------------------------------------------
-// tiled spread: grid[v] += sum_j c[v][perm j] * phase_j * psi-tensor
+// tiled spread, 1-D / 2-D: grid[v] += sum_j c[v][perm j] * phase_j *
+// psi(taps); one thread per point, float shared atomics into an
+// interleaved tile (a 1-D / 2-D point has few taps, and this is the
+// fastest form measured for them).
 template <int DIM, int W>
 __global__ void __launch_bounds__(256)
 k_spread_tiled(const float2* __restrict__ c, int64_t cstride, int nvg,
@@ -361,6 +505,7 @@ k_spread_tiled(const float2* __restrict__ c, int64_t cstride, int nvg,
         for (int q = threadIdx.x; q < nvg * T; q += blockDim.x)
             tile[q] = make_float2(0.0f, 0.0f);
         __syncthreads();
+        {
         for (int base = 0; base < cnt; base += U * blockDim.x) {
             int2 cl[U][DIM];
             int64_t src[U];
@@ -394,6 +539,7 @@ k_spread_tiled(const float2* __restrict__ c, int64_t cstride, int nvg,
                                      l0, wgt, cv);
                 }
             }
+        }
         }
         __syncthreads();
         for (int q = threadIdx.x; q < T; q += blockDim.x) {

@@ -289,3 +289,32 @@ def test_execute_into_host_out_and_launch_count(rng):
     assert p._plan.info().kernel_launches - n0 == 2  # spread, crop (fp32 FFT)
     # spreading accumulates with float atomics: order-dependent rounding
     assert port.rel_l2(out, p.execute(c)) <= 1e-6
+
+
+@pytest.mark.parametrize("upsampfac", [2.0, 1.25])
+def test_staged_execute_and_parallel_stages(upsampfac, rng):
+    """Staged execute (type 1: spread | FFT+crop; type 2: pad+FFT | interp)
+    through mlx_nufft_b200.parallel's single-rank path equals execute();
+    at upsampfac 1.25 the type-2 grid is the fp64-FFT complex128 grid."""
+    import torch
+    from mlx_nufft_b200 import Type1PlanND, Type2PlanND, parallel as par
+    x = pts(rng, 2, 30_000)
+    N = (40, 36)
+    c = rng.standard_normal(30_000) + 1j * rng.standard_normal(30_000)
+    eps = 1e-5    # at upsampfac 1.25 the fp32 floor is above 1e-5
+    p1 = Type1PlanND(tuple(x), N, eps=eps, upsampfac=upsampfac)
+    got1 = par.Type1PointSplit(par.PlanStages(p1)).execute(c).reshape(N)
+    # spreading sums with float atomics, and 1/phihat at upsampfac 1.25
+    # amplifies their order noise: both paths are held to the exact sum
+    exact = fast.direct_t1(x, c, N, +1).reshape(N)
+    assert port.rel_l2(got1, exact) <= gate(eps)
+    assert port.rel_l2(p1.execute(c), exact) <= gate(eps)
+    f = rng.standard_normal(N) + 1j * rng.standard_normal(N)
+    p2 = Type2PlanND(tuple(x), N, eps=eps, upsampfac=upsampfac)
+    st = par.PlanStages(p2)
+    assert st.fp64 == (upsampfac < 1.5)
+    g = st.first(f)
+    assert g.shape == (1,) + tuple(p2.n_up)
+    assert g.dtype == (torch.complex128 if st.fp64 else torch.complex64)
+    got2 = par.Type2TargetSplit(st, 30_000).execute(f)
+    np.testing.assert_array_equal(got2, p2.execute(f))

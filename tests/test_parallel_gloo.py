@@ -1,0 +1,220 @@
+"""Multi-rank orchestration of mlx_nufft_b200.parallel on CPU: two gloo ranks
+(spawned processes, rendezvous on 127.0.0.1) run the same split / collective
+code the GPU ranks run over NCCL, with the plan stages replaced by the CPU
+oracle (oracle/port.py), and the assembled results are checked against the
+single-process oracle on all points.
+
+  * type 1 split by point: per-rank spread grids + all-reduce (or reduce to
+    a root) == spreading all points;
+  * type 2 split by target: root's grid broadcast + per-rank interp,
+    gathered in caller order == interpolating all points;
+  * batched transforms split by vector, gathered == the whole batch;
+  * split_range partitions cover [0, n) exactly once.
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import port
+
+EPS = 1e-6
+TOL = 1e-12     # same fp64 arithmetic on both sides; only summation order differs
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _points(seed, M, dim):
+    rng = np.random.default_rng(seed)
+    return [rng.uniform(-np.pi, np.pi, M) for _ in range(dim)]
+
+
+class OracleT1Stages:
+    """Type-1 stages on the CPU: first = spread (fp64), second = FFT + crop
+    + deconvolution of the (reduced) grid."""
+
+    def __init__(self, x, N, eps, isign):
+        self.N, self.isign = tuple(N), isign
+        self.w, self.beta, self.nup = port.fine_grid_sizes(self.N, eps)
+        self.i1s, self.frs = [], []
+        for d in range(len(x)):
+            i1, fr, _ = port.cells_fold(x[d], self.nup[d], self.w)
+            self.i1s.append(i1)
+            self.frs.append(fr)
+        self.g = None
+
+    def first(self, c):
+        G = port.spread(self.i1s, self.frs, np.asarray(c), self.nup, self.w, self.beta)
+        self.g = torch.from_numpy(np.ascontiguousarray(G))
+        return self.g
+
+    def grid(self):
+        return self.g
+
+    def second(self):
+        V = port._fft(self.g.numpy(), self.isign)
+        N = self.N
+        out = V[np.ix_(*[port._band(N[d], self.nup[d]) for d in range(len(N))])]
+        for d in range(len(N)):
+            k = np.arange(-(N[d] // 2), N[d] - N[d] // 2, dtype=np.float64)
+            dec = 1.0 / port.kernel_ft(2.0 * np.pi * k / self.nup[d], self.beta, self.w)
+            out = out * dec.reshape((1,) * d + (-1,) + (1,) * (len(N) - d - 1))
+        return torch.from_numpy(np.ascontiguousarray(out))
+
+
+class OracleT2Stages:
+    """Type-2 stages on the CPU: first = deconvolve + pad + FFT, second =
+    interp of this rank's points from the (broadcast) grid."""
+
+    def __init__(self, x, N, eps, isign):
+        self.N, self.isign = tuple(N), isign
+        self.w, self.beta, self.nup = port.fine_grid_sizes(self.N, eps)
+        self.i1s, self.frs = [], []
+        for d in range(len(x)):
+            i1, fr, _ = port.cells_fold(x[d], self.nup[d], self.w)
+            self.i1s.append(i1)
+            self.frs.append(fr)
+        self.g = torch.zeros(self.nup, dtype=torch.complex128)
+
+    def first(self, f):
+        f = np.asarray(f, dtype=np.complex128)
+        N = self.N
+        for d in range(len(N)):
+            k = np.arange(-(N[d] // 2), N[d] - N[d] // 2, dtype=np.float64)
+            dec = 1.0 / port.kernel_ft(2.0 * np.pi * k / self.nup[d], self.beta, self.w)
+            f = f * dec.reshape((1,) * d + (-1,) + (1,) * (len(N) - d - 1))
+        H = np.zeros(self.nup, dtype=np.complex128)
+        H[np.ix_(*[port._band(N[d], self.nup[d]) for d in range(len(N))])] = f
+        self.g.copy_(torch.from_numpy(port._fft(H, self.isign)))
+        return self.g
+
+    def grid(self):
+        return self.g
+
+    def second(self):
+        return torch.from_numpy(port.interp(self.g.numpy(), self.i1s, self.frs,
+                                            self.w, self.beta))
+
+
+class OracleBatchPlan:
+    """execute_batch of type 1 on the CPU oracle (one call per vector)."""
+
+    def __init__(self, x, N, eps, isign):
+        self.x, self.N, self.eps, self.isign = x, N, eps, isign
+
+    def execute_batch(self, cs, return_np=False):
+        res = np.stack([port.nufft_t1(self.x, np.asarray(c), self.N, self.eps,
+                                      self.isign) for c in cs])
+        return torch.from_numpy(res)
+
+
+def _worker(rank, world, port_, case, queue):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port_)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from mlx_nufft_b200 import parallel as par
+        out = None
+        if case in ("t1", "t1_root"):
+            M, N = 3000, (24, 20)
+            x = _points(1, M, 2)
+            c = np.random.default_rng(2).standard_normal(M) + 0j
+            lo, hi = par.split_range(M, rank, world)
+            st = OracleT1Stages([v[lo:hi] for v in x], N, EPS, +1)
+            root = 0 if case == "t1_root" else None
+            r = par.Type1PointSplit(st, root=root).execute(c[lo:hi])
+            out = None if r is None else np.asarray(r)
+        elif case == "t2":
+            M, N = 2500, (16, 18)
+            x = _points(3, M, 2)
+            rng = np.random.default_rng(4)
+            f = rng.standard_normal(N) + 1j * rng.standard_normal(N)
+            lo, hi = par.split_range(M, rank, world)
+            st = OracleT2Stages([v[lo:hi] for v in x], N, EPS, -1)
+            # only the root's modes matter: the others pass garbage
+            mine = f if rank == 0 else np.full(N, np.nan)
+            out = np.asarray(par.Type2TargetSplit(st, M).execute(mine, gather=True))
+        elif case == "batch":
+            M, N, B = 800, (12,), 5
+            x = _points(5, M, 1)
+            cs = np.random.default_rng(6).standard_normal((B, M)) + 0j
+            sb = par.ShardedBatch(OracleBatchPlan(x, N, EPS, +1))
+            lo, hi = sb.local_range(B)
+            out = (lo, hi, np.asarray(sb.execute_batch(cs, gather=True)))
+        queue.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(case, world=2):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port_ = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port_, case, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    return res
+
+
+def test_split_range_partitions():
+    from mlx_nufft_b200.parallel import split_range
+    for n in (0, 1, 7, 8, 1000):
+        for world in (1, 2, 3, 8):
+            spans = [split_range(n, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            sizes = [hi - lo for lo, hi in spans]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        split_range(10, 2, 2)
+
+
+@pytest.mark.parametrize("case", ["t1", "t1_root"])
+def test_type1_point_split_allreduce(case):
+    res = _run(case)
+    M, N = 3000, (24, 20)
+    x = _points(1, M, 2)
+    c = np.random.default_rng(2).standard_normal(M) + 0j
+    ref = port.nufft_t1(x, c, N, EPS, +1)
+    if case == "t1":
+        for r in (0, 1):
+            assert port.rel_l2(res[r], ref) <= TOL
+    else:
+        assert port.rel_l2(res[0], ref) <= TOL and res[1] is None
+
+
+def test_type2_target_split_broadcast():
+    res = _run("t2")
+    M, N = 2500, (16, 18)
+    x = _points(3, M, 2)
+    rng = np.random.default_rng(4)
+    f = rng.standard_normal(N) + 1j * rng.standard_normal(N)
+    ref = port.nufft_t2(x, f, EPS, -1)
+    for r in (0, 1):
+        assert np.all(np.isfinite(res[r]))
+        assert port.rel_l2(res[r], ref) <= TOL
+
+
+def test_batch_split_by_vector():
+    res = _run("batch")
+    M, N, B = 800, (12,), 5
+    x = _points(5, M, 1)
+    cs = np.random.default_rng(6).standard_normal((B, M)) + 0j
+    ref = np.stack([port.nufft_t1(x, c, N, EPS, +1) for c in cs])
+    assert res[0][:2] == (0, 3) and res[1][:2] == (3, 5)
+    for r in (0, 1):
+        assert port.rel_l2(res[r][2], ref) <= TOL
