@@ -52,6 +52,7 @@ void es_poly_coeffs(int w, double beta, int deg, float* coef);
 
 // Kernel-width limits and the polynomial degree used for width W.
 constexpr int kMaxW = 16;
+constexpr int kMaxTapRounds = 4;      // ceil(W^2 / 32) for W <= 10
 constexpr int kMaxDeg = kMaxW + 2;
 __host__ __device__ constexpr int es_degree(int w) { return w + 2; }
 
@@ -107,6 +108,12 @@ struct TileGeom {
     float beta;           // (float) beta
     int keval;            // 1: polynomial weights, 0: exp/sqrt per tap
     EsPoly poly;          // ES kernel as per-tap polynomials in fr
+    // 3-D plane-owned spreading (k_spread_planes): shared row stride S2 >= T[2]
+    // and, per round r and lane l, the in-plane tap (y << 4 | x) of lane l
+    // (0xff: idle), chosen so each half-warp's 16 accesses hit 16 distinct
+    // 8-byte bank pairs; rounds = ceil(W^2 / 32).
+    int S2;
+    uint8_t tapmap[kMaxTapRounds * 32];
 };
 
 // One sorted (or caller-ordered) set of nonuniform points on the device.

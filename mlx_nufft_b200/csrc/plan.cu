@@ -161,6 +161,51 @@ int env_int(const char* name, int dflt) {
 }
 
 // ----------------------------------------------------------------------
+// In-plane tap order of the 3-D plane-owned spread (k_spread_planes): lanes
+// of a half-warp read / write 16 float2 at tile offsets y*S2 + x; they use
+// 16 distinct bank pairs when those offsets are distinct mod 16.  Greedy
+// fill of half-warps with taps of distinct residues, for the smallest row
+// stride S2 >= T2 (up to T2 + 8) that needs only ceil(W^2 / 32) rounds;
+// otherwise the plain order at S2 = T2 (correct, with bank conflicts).
+void plane_tap_order(TileGeom& tg, int w) {
+    std::memset(tg.tapmap, 0xff, sizeof(tg.tapmap));
+    const int T2 = tg.T[2];
+    const int rounds = (w * w + 31) / 32;
+    tg.S2 = T2;
+    if (w > kMaxW || rounds > kMaxTapRounds) return;
+    for (int S = T2; S <= T2 + 8; ++S) {
+        std::vector<int> left;
+        for (int t = 0; t < w * w; ++t) left.push_back(t);
+        std::vector<std::vector<int>> halves;
+        while (!left.empty()) {
+            std::vector<int> half, rest;
+            bool used[16] = {};
+            for (int t : left) {
+                const int r = ((t / w) * S + t % w) % 16;
+                if (!used[r] && half.size() < 16) {
+                    used[r] = true;
+                    half.push_back(t);
+                } else {
+                    rest.push_back(t);
+                }
+            }
+            halves.push_back(half);
+            left.swap(rest);
+        }
+        if ((int)(halves.size() + 1) / 2 > rounds) continue;
+        for (size_t h = 0; h < halves.size(); ++h)
+            for (size_t i = 0; i < halves[h].size(); ++i) {
+                const int t = halves[h][i];
+                tg.tapmap[h * 16 + i] = (uint8_t)(((t / w) << 4) | (t % w));
+            }
+        tg.S2 = S;
+        return;
+    }
+    for (int t = 0; t < w * w; ++t)
+        tg.tapmap[t] = (uint8_t)(((t / w) << 4) | (t % w));
+}
+
+// ----------------------------------------------------------------------
 // tiling choice per grid: bin extent m per dimension so that the tile
 // (m + w - 1)^dim of complex64 fits shared memory with room for several
 // vectors.  1-D bins are 4096 cells for interpolation (each subproblem
@@ -197,6 +242,8 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
         tg.tdiv[d] = tg.T[d] > 1
             ? (uint32_t)(((uint64_t)1 << 32) / (uint64_t)tg.T[d] + 1) : 0u;
     }
+    tg.S2 = tg.T[2];
+    if (dim == 3) plane_tap_order(tg, w);
     return tg;
 }
 

@@ -50,15 +50,20 @@ int persistent_grid(const void* kernel, size_t smem, int64_t work, int threads) 
 
 void ensure_smem(const void* kernel, size_t bytes) {
     static std::mutex mu;
+    static std::map<const void*, size_t> statics;  // kernel -> static bytes
     static std::map<const void*, size_t> raised;   // kernel -> limit set
-    if (bytes <= 48 * 1024) return;
     std::lock_guard<std::mutex> lk(mu);
+    auto st = statics.find(kernel);
+    if (st == statics.end()) {
+        cudaFuncAttributes fa{};
+        NUFFT_CUDA(cudaFuncGetAttributes(&fa, kernel));
+        st = statics.emplace(kernel, (size_t)fa.sharedSizeBytes).first;
+    }
+    // without the opt-in, static + dynamic shared memory is limited to 48 KB
+    if (bytes + st->second <= 48 * 1024) return;
     auto it = raised.find(kernel);
     if (it != raised.end() && it->second >= bytes) return;
-    // the dynamic limit excludes the kernel's static shared memory
-    cudaFuncAttributes fa{};
-    NUFFT_CUDA(cudaFuncGetAttributes(&fa, kernel));
-    const size_t cap = (size_t)tile_smem_limit() - fa.sharedSizeBytes;
+    const size_t cap = (size_t)tile_smem_limit() - st->second;
     if (bytes > cap) fail(-1, "tile does not fit in shared memory");
     NUFFT_CUDA(cudaFuncSetAttribute(
         kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cap));
@@ -75,7 +80,7 @@ void launch_planes(const PointSet& ps, const TileGeom& tg, const float2* c,
                    int64_t cstride, const uint32_t* perm, const CellPtrs& cells,
                    float2* grid, cudaStream_t st) {
     auto k = k_spread_planes<W, NV>;
-    const size_t smem = (size_t)NV * tg.tcells * sizeof(float2);
+    const size_t smem = (size_t)NV * tg.T[0] * tg.T[1] * tg.S2 * sizeof(float2);
     ensure_smem((const void*)k, smem);
     const int blocks = persistent_grid((const void*)k, smem, ps.nsub,
                                        32 * kPlaneWarps);
@@ -95,7 +100,7 @@ void spread_impl(const PointSet& ps, const TileGeom& tg, const float2* c,
         if (ps.nsub == 0) return;
         if constexpr (DIM == 3 && W <= 10) {
             // groups of 4, 2 or 1 vectors, each group's tile within 96 KB
-            const size_t per = (size_t)tg.tcells * sizeof(float2);
+            const size_t per = (size_t)tg.T[0] * tg.T[1] * tg.S2 * sizeof(float2);
             for (int v0 = 0; v0 < nvec;) {
                 const int left = nvec - v0;
                 const int nv = (left >= 4 && 4 * per <= kPlaneTileBudget) ? 4

@@ -342,6 +342,9 @@ __host__ __device__ constexpr int batch_u() {
 // W <= 8 consecutive planes, i.e. at most one plane per warp (W > 8: at
 // most two), and within a plane the lanes take distinct (y, x) taps.
 // __syncwarp() orders one point's stores before the next point's loads.
+// The in-plane taps are spread over the lanes by the plan's table
+// (TileGeom::tapmap) with the shared rows padded to stride S2, so the 16
+// accesses of each half-warp fall on distinct bank pairs.
 //
 // Points are staged 128 at a time: one thread per point computes its tile
 // offset, its 3 x W kernel weights and its NV strengths (times the phase)
@@ -360,23 +363,27 @@ k_spread_planes(const float2* __restrict__ c, int64_t cstride,
                 TileGeom tg) {
     constexpr int W2 = W * W;
     constexpr int NR = (W2 + 31) / 32;               // rounds per plane
-    extern __shared__ float2 tile[];                 // [NV][T]
+    static_assert(NR <= kMaxTapRounds, "tap table too small");
+    extern __shared__ float2 tile[];                 // [NV][T0][T1][S2]
     __shared__ int s_l0[kPlaneChunk];                // l0z, tile offset of (l0z, l0y, l0x)
     __shared__ int s_off[kPlaneChunk];
     __shared__ float s_w[kPlaneChunk][3 * W];
     __shared__ float2 s_c[kPlaneChunk][NV];
     __shared__ int s_sub;
     const int T = tg.tcells;
-    const int T2 = tg.T[2], TT = tg.T[1] * tg.T[2];
+    const int S2 = tg.S2, TT = tg.T[1] * tg.S2;
+    const int TS = tg.T[0] * TT;                     // padded cells per vector
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     // this lane's (y, x) tap in each round and its offset inside a plane
     int rb[NR], rk[NR], roff[NR];
+    bool ract[NR];
 #pragma unroll
     for (int r = 0; r < NR; ++r) {
-        const int t = min(r * 32 + lane, W2 - 1);
-        rb[r] = t / W;
-        rk[r] = t - rb[r] * W;
-        roff[r] = rb[r] * T2 + rk[r];
+        const int m = tg.tapmap[r * 32 + lane];
+        ract[r] = m != 0xff;
+        rb[r] = ract[r] ? (m >> 4) : 0;
+        rk[r] = ract[r] ? (m & 15) : 0;
+        roff[r] = rb[r] * S2 + rk[r];
     }
     for (;;) {
         const int sub = next_subproblem(sched, &s_sub);    // (syncs)
@@ -385,7 +392,7 @@ k_spread_planes(const float2* __restrict__ c, int64_t cstride,
         const int start = sb.x, cnt = sb.y;
         int o[3] = {0, 0, 0};
         bin_origin<3>(sb.z, tg, o);
-        for (int q = threadIdx.x; q < NV * T; q += blockDim.x)
+        for (int q = threadIdx.x; q < NV * TS; q += blockDim.x)
             tile[q] = make_float2(0.0f, 0.0f);
         for (int c0 = 0; c0 < cnt; c0 += kPlaneChunk) {
             const int n = min(kPlaneChunk, cnt - c0);
@@ -408,7 +415,7 @@ k_spread_planes(const float2* __restrict__ c, int64_t cstride,
                 // l0z = -1 marks a point outside the bin (never for
                 // consistent setpts output): every warp skips it
                 s_l0[p] = ok ? l0[0] : -1;
-                s_off[p] = l0[1] * T2 + l0[2];
+                s_off[p] = l0[1] * S2 + l0[2];
                 const int64_t src = perm ? (int64_t)__ldg(perm + j) : j;
                 const float2 ph = phase ? __ldg(phase + j) : make_float2(1.0f, 0.0f);
 #pragma unroll
@@ -442,17 +449,17 @@ k_spread_planes(const float2* __restrict__ c, int64_t cstride,
                     float2 g[NR][NV];
 #pragma unroll
                     for (int r = 0; r < NR; ++r)
-                        if (r * 32 + lane < W2)
+                        if (ract[r])
 #pragma unroll
-                            for (int v = 0; v < NV; ++v) g[r][v] = tile[v * T + q[r]];
+                            for (int v = 0; v < NV; ++v) g[r][v] = tile[v * TS + q[r]];
 #pragma unroll
                     for (int r = 0; r < NR; ++r)
-                        if (r * 32 + lane < W2)
+                        if (ract[r])
 #pragma unroll
                             for (int v = 0; v < NV; ++v) {
                                 g[r][v].x = fmaf(cv[v].x, wr[r], g[r][v].x);
                                 g[r][v].y = fmaf(cv[v].y, wr[r], g[r][v].y);
-                                tile[v * T + q[r]] = g[r][v];
+                                tile[v * TS + q[r]] = g[r][v];
                             }
                 }
                 __syncwarp();
@@ -461,9 +468,12 @@ k_spread_planes(const float2* __restrict__ c, int64_t cstride,
         __syncthreads();
         for (int q = threadIdx.x; q < T; q += blockDim.x) {
             const int64_t g = tile_to_global<3>(q, o, tg);
+            // shared index of tile cell q: row q / T2 at stride S2
+            const int row = (int)__umulhi((unsigned)q, tg.tdiv[2]);
+            const int sq = row * S2 + (q - row * tg.T[2]);
 #pragma unroll
             for (int v = 0; v < NV; ++v) {
-                const float2 val = tile[v * T + q];
+                const float2 val = tile[v * TS + sq];
                 if (val.x != 0.0f || val.y != 0.0f)
                     atomicAdd(grid + v * tg.ncells + g, val);
             }
