@@ -26,8 +26,8 @@ INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 LIB = os.path.join(HERE, "libnufft_b200.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["sizing.cpp", "points.cu", "spread.cu", "interp.cu", "deconv.cu",
-           "plan.cu", "noalloc.cu"]
+SOURCES = ["sizing.cpp", "points.cu", "spread.cu", "interp.cu", "interp_tma.cu",
+           "deconv.cu", "plan.cu", "noalloc.cu"]
 
 
 def _cuda_home():

@@ -6,6 +6,7 @@
 #include <string>
 #include <vector>
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace nufft {
@@ -179,6 +180,19 @@ void launch_spread(const PointSet& ps, const TileGeom& tg, int w,
 // Interpolate nvec grids (complex64, or complex128 when grid64) at the
 // points into out (vector stride ostride), multiplying by ps.phase when
 // present.
+// 3-D interpolation with TMA-staged tiles (interp_tma.cu): the tensor map
+// over a plan's nbatch complex64 fine grids, and the launcher (false: not
+// applicable, use launch_interp).
+bool make_grid_tmap(CUtensorMap* map, const float2* grid, const TileGeom& tg,
+                    int nbatch);
+bool launch_interp_tma(const PointSet& ps, const TileGeom& tg, int w,
+                       const CUtensorMap* map, const float2* grid, int nvec,
+                       float2* out, int64_t ostride, int* err, cudaStream_t st);
+// plan error-flag bits (device int): non-finite coordinate, tile-copy wait
+// timed out
+constexpr int kErrNonFinite = 1;
+constexpr int kErrTileWait = 4;
+
 void launch_interp(const PointSet& ps, const TileGeom& tg, int w,
                    const void* grid, bool grid64, int nvec, float2* out,
                    int64_t ostride, int nvg, cudaStream_t st);

@@ -1,0 +1,367 @@
+// interp_tma.cu -- 3-D tiled interpolation with TMA-staged, double-buffered
+// grid tiles (types 2 and 3, complex64 fine grid).
+//
+// The plain tiled kernel (k_interp_tiled) loads each subproblem's tile with
+// per-thread loads (index arithmetic per cell, then a barrier) before any
+// point can be processed; in 3-D at low density (tens of points per 8^3
+// bin, e.g. the uniform half of a clustered set) that load dominates.  Here
+// one thread issues the whole tile as one bulk tensor copy per vector
+// (cp.async.bulk.tensor, completion on an mbarrier) for the NEXT
+// subproblem while the CTA interpolates the current one from the other
+// buffer.
+//
+// Tensor map: the plan's nbatch fine grids as a 4-D array (x, y, z, vector)
+// of 8-byte elements (complex64).  A TMA copy must start at a 16-byte
+// boundary in x, so each tile box starts at the even cell x0 = o_x rounded
+// down and is B2 = T2 + 1 rounded up to even cells wide; the point
+// arithmetic adds the offset o_x - x0 (0 or 1).  Bins whose tile would
+// wrap around the periodic grid (the box is not inside [0, n)) are loaded
+// by the CTA's threads with wrap, into the same padded layout.
+//
+// Every mbarrier wait is bounded: after kSpinLimit polls the CTA records
+// an error in err[0], waits (bounded again) for its other copy in flight,
+// and stops.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "spreadinterp.cuh"
+
+namespace nufft {
+
+namespace {
+
+constexpr int kSpinLimit = 1 << 22;
+
+#ifndef NUFFT_TMA_MINB
+#define NUFFT_TMA_MINB 3
+#endif
+
+__host__ __device__ __forceinline__ int tma_buffer_cells(const TileGeom& tg, int B2) {
+    return ((tg.T[0] * tg.T[1] * B2) + 15) & ~15;
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile(
+        "mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+        "r"(bytes)
+        : "memory");
+}
+
+// true when the phase with parity `parity` has completed; bounded polling
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    const uint32_t a = smem_addr(bar);
+    for (int it = 0; it < kSpinLimit; ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map,
+                                            int x, int y, int z, int v,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_addr(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(v), "r"(smem_addr(bar))
+        : "memory");
+}
+
+struct TmaBin {
+    int o[3];        // tile origin (global cell of tile index 0), per dim
+    int x0;          // box start in x (even)
+    bool interior;   // box inside the grid: TMA-loadable
+};
+
+__device__ __forceinline__ TmaBin tma_bin(int bin, const TileGeom& tg, int B2,
+                                          bool use_tma) {
+    TmaBin b;
+    bin_origin<3>(bin, tg, b.o);
+    b.x0 = b.o[2] - (b.o[2] & 1);
+    b.interior = use_tma && b.o[0] >= 0 && b.o[0] + tg.T[0] <= tg.n[0] &&
+                 b.o[1] >= 0 && b.o[1] + tg.T[1] <= tg.n[1] &&
+                 b.x0 >= 0 && b.x0 + B2 <= tg.n[2];
+    return b;
+}
+
+// taps of one point from a padded tile: rows of stride S (cells), planes
+// of T1 * S; `base` is the tile index of the point's first tap
+template <int W>
+__device__ __forceinline__ float2 gather3(const float2* tv, int S, int PS,
+                                          int base, float (&wgt)[3][W]) {
+    float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll 1
+    for (int a = 0; a < W; ++a, base += PS) {
+        float2 sa = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int b = 0; b < W; ++b) {
+            const float2* row = tv + base + b * S;
+            float2 s = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int k = 0; k < W; ++k) {
+                const float2 g = row[k];
+                s.x = fmaf(g.x, wgt[2][k], s.x);
+                s.y = fmaf(g.y, wgt[2][k], s.y);
+            }
+            sa.x = fmaf(s.x, wgt[1][b], sa.x);
+            sa.y = fmaf(s.y, wgt[1][b], sa.y);
+        }
+        acc.x = fmaf(sa.x, wgt[0][0], acc.x);
+        acc.y = fmaf(sa.y, wgt[0][0], acc.y);
+        rotate<W>(wgt[0]);
+    }
+    return acc;
+}
+
+template <int W>
+__global__ void __launch_bounds__(256, NUFFT_TMA_MINB)
+k_interp_tma(const __grid_constant__ CUtensorMap tmap, const float2* __restrict__ grid,
+             int v0, int nvg, int B2, const uint32_t* __restrict__ perm,
+             CellPtrs cells, const float2* __restrict__ phase,
+             const int4* __restrict__ subs, int nsub, int* __restrict__ sched,
+             float2* __restrict__ out, int64_t ostride, TileGeom tg,
+             int* __restrict__ err) {
+    extern __shared__ __align__(128) float2 sbuf[];     // [2][nvg][T0][T1][B2]
+    __shared__ __align__(8) uint64_t bar[2];
+    __shared__ int s_next;
+    __shared__ int s_tma;                                // 0: all tiles by hand
+    constexpr int U = 2;
+    const int S = B2, PS = tg.T[1] * B2;
+    // cells per vector buffer, rounded to 16 cells: every TMA destination
+    // is 128-byte aligned
+    const int TS = tma_buffer_cells(tg, B2);
+    const uint32_t tile_bytes = (uint32_t)(tg.T[0] * PS) * sizeof(float2);
+    const uint64_t pol = l2_evict_last_policy();
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        s_next = atomicAdd(&sched[0], 1);
+        s_tma = (smem_addr(sbuf) & 127u) == 0;
+    }
+    __syncthreads();
+    const bool use_tma = s_tma != 0;
+    auto issue = [&](const TmaBin& bn, int b) {
+        // thread 0: this CTA's generic-proxy reads of buffer b are ordered
+        // before the async-proxy writes by the preceding barrier + fence
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect_tx(&bar[b], tile_bytes * (uint32_t)nvg);
+        for (int v = 0; v < nvg; ++v)
+            tma_load_4d(sbuf + ((size_t)b * nvg + v) * TS, &tmap, bn.x0, bn.o[1],
+                        bn.o[0], v0 + v, &bar[b]);
+    };
+    int cur = s_next;
+    int b = 0;
+    uint32_t parity[2] = {0u, 0u};
+    bool pending[2] = {false, false};
+    if (cur < nsub && threadIdx.x == 0) {
+        const TmaBin bn = tma_bin(subs[cur].z, tg, B2, use_tma);
+        if (bn.interior) issue(bn, 0);
+    }
+    if (cur < nsub) pending[0] = tma_bin(subs[cur].z, tg, B2, use_tma).interior;
+    bool failed = false;
+    while (cur < nsub) {
+        __syncthreads();                        // previous s_next consumed
+        if (threadIdx.x == 0) s_next = atomicAdd(&sched[0], 1);
+        __syncthreads();
+        const int nxt = s_next;
+        if (nxt < nsub) {
+            const TmaBin nb = tma_bin(subs[nxt].z, tg, B2, use_tma);
+            pending[b ^ 1] = nb.interior;
+            if (nb.interior && threadIdx.x == 0) issue(nb, b ^ 1);
+        }
+        const int4 sb = subs[cur];
+        const TmaBin bn = tma_bin(sb.z, tg, B2, use_tma);
+        float2* tile = sbuf + (size_t)b * nvg * TS;
+        int xoff;
+        if (bn.interior) {
+            const bool ok = mbar_wait(&bar[b], parity[b]);
+            parity[b] ^= 1u;
+            pending[b] = false;
+            if (__syncthreads_or(!ok)) {
+                failed = true;
+                break;
+            }
+            xoff = bn.o[2] - bn.x0;
+        } else {
+            // wrapped tile: per-thread loads into the same padded layout
+            for (int q = threadIdx.x; q < tg.tcells; q += blockDim.x) {
+                const int64_t g = tile_to_global<3>(q, bn.o, tg);
+                const int row = (int)__umulhi((unsigned)q, tg.tdiv[2]);
+                const int sq = row * S + (q - row * tg.T[2]);
+                for (int v = 0; v < nvg; ++v)
+                    tile[v * TS + sq] = grid[(int64_t)(v0 + v) * tg.ncells + g];
+            }
+            __syncthreads();
+            xoff = 0;
+        }
+        const int start = sb.x, cnt = sb.y;
+        for (int base = 0; base < cnt; base += U * blockDim.x) {
+            int2 cl[U][3];
+            int64_t dst[U];
+            float2 ph[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int t = base + u * blockDim.x + threadIdx.x;
+                const int64_t j = start + min(t, cnt - 1);
+#pragma unroll
+                for (int d = 0; d < 3; ++d) cl[u][d] = __ldcs(cells.d[d] + j);
+                dst[u] = perm ? (int64_t)__ldcs(perm + j) : j;
+                ph[u] = phase ? __ldcs(phase + j) : make_float2(1.0f, 0.0f);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                if (base + u * (int)blockDim.x + (int)threadIdx.x >= cnt) break;
+                float wgt[3][W];
+                int l0[3];
+                bool ok = true;
+#pragma unroll
+                for (int d = 0; d < 3; ++d) {
+                    l0[d] = cl[u][d].x - bn.o[d];
+                    ok &= (unsigned)l0[d] < (unsigned)tg.m[d];
+                    kernel_weights<W>(__int_as_float(cl[u][d].y), tg, wgt[d]);
+                }
+                const int tb = l0[0] * PS + l0[1] * S + l0[2] + xoff;
+                for (int v = 0; v < nvg; ++v) {
+                    // gather3 rotates the x-weights W times: back in order
+                    float2 acc = make_float2(0.0f, 0.0f);
+                    if (ok) {
+                        acc = gather3<W>(tile + v * TS, S, PS, tb, wgt);
+                        if (phase) acc = cmul(acc, ph[u]);
+                    }
+                    if (perm)
+                        st_keep(out + v * ostride + dst[u], acc, pol);
+                    else
+                        out[v * ostride + dst[u]] = acc;
+                }
+            }
+        }
+        cur = nxt;
+        b ^= 1;
+    }
+    if (failed && threadIdx.x == 0) {
+        atomicOr(err, kErrTileWait);
+        // the other buffer may still have a copy in flight: wait for it
+        // (bounded) before the CTA's shared memory is released
+        const int o = b ^ 1;
+        if (pending[o]) mbar_wait(&bar[o], parity[o]);
+    }
+    scheduler_done(sched);
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no
+// libcuda link); null when the driver does not provide it.
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
+                                 void*, const cuuint64_t*, const cuuint64_t*,
+                                 const cuuint32_t*, const cuuint32_t*,
+                                 CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_tiled() {
+    static std::once_flag once;
+    static EncodeTiled fn = nullptr;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault,
+                                    &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiled)p;
+        cudaGetLastError();
+    });
+    return fn;
+}
+
+}  // namespace
+
+int tma_box_x(const TileGeom& tg) {
+    return (tg.T[2] + 2) & ~1;          // T2 + 1 rounded up to even
+}
+
+bool make_grid_tmap(CUtensorMap* map, const float2* grid, const TileGeom& tg,
+                    int nbatch) {
+    if (tg.dim != 3) return false;
+    EncodeTiled enc = encode_tiled();
+    if (!enc) return false;
+    const int B2 = tma_box_x(tg);
+    if (B2 > 256 || tg.T[1] > 256 || tg.T[0] > 256 || B2 > tg.n[2]) return false;
+    const cuuint64_t dims[4] = {(cuuint64_t)tg.n[2], (cuuint64_t)tg.n[1],
+                                (cuuint64_t)tg.n[0], (cuuint64_t)nbatch};
+    const cuuint64_t strides[3] = {(cuuint64_t)tg.n[2] * 8,
+                                   (cuuint64_t)tg.n[1] * tg.n[2] * 8,
+                                   (cuuint64_t)tg.ncells * 8};
+    const cuuint32_t box[4] = {(cuuint32_t)B2, (cuuint32_t)tg.T[1],
+                               (cuuint32_t)tg.T[0], 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, (void*)grid, dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int W>
+void interp_tma_impl(const PointSet& ps, const TileGeom& tg, const CUtensorMap& map,
+                     const float2* grid, int nvec, float2* out, int64_t ostride,
+                     int nvg, int* err, cudaStream_t st) {
+    auto k = k_interp_tma<W>;
+    const int B2 = tma_box_x(tg);
+    const size_t per = (size_t)tma_buffer_cells(tg, B2) * sizeof(float2);
+    for (int v0 = 0; v0 < nvec; v0 += nvg) {
+        const int nv = std::min(nvg, nvec - v0);
+        const size_t smem = 2 * nv * per;
+        ensure_smem((const void*)k, smem);
+        const int blocks = persistent_grid((const void*)k, smem, ps.nsub);
+        k<<<blocks, 256, smem, st>>>(map, grid, v0, nv, B2,
+                                     ps.sorted ? ps.perm : nullptr, cell_ptrs(ps),
+                                     ps.phase, ps.subs, (int)ps.nsub, ps.sched,
+                                     out + v0 * ostride, ostride, tg, err);
+        NUFFT_LAUNCH("k_interp_tma");
+    }
+}
+
+bool launch_interp_tma(const PointSet& ps, const TileGeom& tg, int w,
+                       const CUtensorMap* map, const float2* grid, int nvec,
+                       float2* out, int64_t ostride, int* err, cudaStream_t st) {
+    if (!map || !ps.tiled || ps.dim != 3 || w > 10) return false;
+    if (ps.nsub == 0) return true;
+    // two buffers of up to nvg vectors within ~100 KB: two CTAs per SM
+    const size_t per = (size_t)tma_buffer_cells(tg, tma_box_x(tg)) * sizeof(float2);
+    const int nvg = (int)std::max<size_t>(1, (100 * 1024) / (2 * per));
+    if (2 * per > (size_t)tile_smem_limit() - 4096) return false;
+    switch (w) {
+        case 2: interp_tma_impl<2>(ps, tg, *map, grid, nvec, out, ostride, nvg, err, st); break;
+        case 3: interp_tma_impl<3>(ps, tg, *map, grid, nvec, out, ostride, nvg, err, st); break;
+        case 4: interp_tma_impl<4>(ps, tg, *map, grid, nvec, out, ostride, nvg, err, st); break;
+        case 5: interp_tma_impl<5>(ps, tg, *map, grid, nvec, out, ostride, nvg, err, st); break;
+        case 6: interp_tma_impl<6>(ps, tg, *map, grid, nvec, out, ostride, nvg, err, st); break;
+        case 7: interp_tma_impl<7>(ps, tg, *map, grid, nvec, out, ostride, nvg, err, st); break;
+        case 8: interp_tma_impl<8>(ps, tg, *map, grid, nvec, out, ostride, nvg, err, st); break;
+        case 9: interp_tma_impl<9>(ps, tg, *map, grid, nvec, out, ostride, nvg, err, st); break;
+        case 10: interp_tma_impl<10>(ps, tg, *map, grid, nvec, out, ostride, nvg, err, st); break;
+        default: return false;
+    }
+    return true;
+}
+
+}  // namespace nufft

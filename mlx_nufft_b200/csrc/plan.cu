@@ -149,6 +149,13 @@ struct nufft_plan_s {
     int* d_err = nullptr;
     int64_t launches = 0;      // own kernels launched by executes
     int64_t fft_execs = 0;     // cuFFT executions issued by executes
+    // TMA tensor map over the complex64 FFT grids for the 3-D interpolation,
+    // valid for (tmap_grid, tmap_nbatch, tmap_n)
+    CUtensorMap tmap{};
+    const void* tmap_grid = nullptr;
+    int tmap_nbatch = 0;
+    int tmap_n[3] = {0, 0, 0};
+    bool tmap_ok = false;
 };
 
 namespace nufft_impl {
@@ -391,6 +398,9 @@ void check_err_flag(nufft_plan_s* p, cudaStream_t st) {
     if (h) {
         NUFFT_CUDA(cudaMemsetAsync(p->d_err, 0, sizeof(int), st));
         NUFFT_CUDA(cudaStreamSynchronize(st));
+        if (h & kErrTileWait)
+            fail(NUFFT_ERR_CUDA, "an interpolation tile copy did not complete "
+                                 "(earlier execute results are invalid)");
         fail(NUFFT_ERR_ARG, "non-finite nonuniform coordinate");
     }
 }
@@ -654,6 +664,22 @@ void setpts_t3(nufft_plan_s* p, int64_t M, const double* const* xs, int64_t N,
 }
 
 // ---------------------------------------------------------------------
+// Tensor map for the TMA-staged 3-D interpolation from the FFT grids
+// (complex64 only), re-encoded when the grids or the tile geometry change;
+// null when not applicable.  NUFFT_INTERP_TMA=0 disables the path (tuning).
+const CUtensorMap* interp_tmap(nufft_plan_s* p, const TileGeom& tg) {
+    static const int on = env_int("NUFFT_INTERP_TMA", 1);
+    if (!on || p->fft64 || tg.dim != 3) return nullptr;
+    if (p->tmap_grid != p->gfft || p->tmap_nbatch != p->nbatch ||
+        p->tmap_n[0] != tg.n[0] || p->tmap_n[1] != tg.n[1] || p->tmap_n[2] != tg.n[2]) {
+        p->tmap_ok = make_grid_tmap(&p->tmap, p->gfft, tg, p->nbatch);
+        p->tmap_grid = p->gfft;
+        p->tmap_nbatch = p->nbatch;
+        for (int d = 0; d < 3; ++d) p->tmap_n[d] = tg.n[d];
+    }
+    return p->tmap_ok ? &p->tmap : nullptr;
+}
+
 void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
                    int stage, cudaStream_t st) {
     if (p->type == 1) {
@@ -697,8 +723,10 @@ void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
             record(p, 1, st);
             record(p, 2, st);
         }
-        launch_interp(p->src, p->tg_src, p->w, p->gfft, p->fft64, nv, out,
-                      p->src.M, p->nvg_src, st);
+        if (!launch_interp_tma(p->src, p->tg_src, p->w, interp_tmap(p, p->tg_src),
+                               p->gfft, nv, out, p->src.M, p->d_err, st))
+            launch_interp(p->src, p->tg_src, p->w, p->gfft, p->fft64, nv, out,
+                          p->src.M, p->nvg_src, st);
         record(p, 3, st);
     } else {
         record(p, 0, st);
@@ -710,8 +738,10 @@ void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
         record(p, 1, st);
         run_fft(p, nv, st);
         record(p, 2, st);
-        launch_interp(p->tgt, p->tg_tgt, p->w2, p->gfft, p->fft64, nv, out,
-                      p->Ntgt, p->nvg_tgt, st);
+        if (!launch_interp_tma(p->tgt, p->tg_tgt, p->w2, interp_tmap(p, p->tg_tgt),
+                               p->gfft, nv, out, p->Ntgt, p->d_err, st))
+            launch_interp(p->tgt, p->tg_tgt, p->w2, p->gfft, p->fft64, nv, out,
+                          p->Ntgt, p->nvg_tgt, st);
         record(p, 3, st);
     }
     p->ev_recorded = p->profile;
