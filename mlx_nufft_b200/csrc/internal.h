@@ -117,6 +117,14 @@ struct TileGeom {
     uint8_t tapmap[kMaxTapRounds * 32];
 };
 
+// Elements allocated past M in every per-point array (cells, permutation,
+// phases): 16-byte-aligned bulk copies of a subproblem's range may read up
+// to 3 elements beyond its end.
+constexpr int64_t kPointSlack = 16;
+// Largest subproblem (points) of the 1-D streamed interpolation, whose
+// shared-memory stage holds a subproblem's cells and permutation.
+constexpr int kStreamMsubMax = 2048;
+
 // One sorted (or caller-ordered) set of nonuniform points on the device.
 struct PointSet {
     int dim = 0;
@@ -125,6 +133,7 @@ struct PointSet {
     uint32_t* perm = nullptr;   // sorted position -> caller index (null: identity)
     int4* subs = nullptr;       // (start, count, bin, 0) per subproblem
     int64_t nsub = 0;
+    int msub = 0;               // points per subproblem at most
     int64_t cap = 0;            // allocated points
     int64_t subcap = 0;         // allocated subproblems
     float2* phase = nullptr;    // type 3: prephase / postphase, sorted order

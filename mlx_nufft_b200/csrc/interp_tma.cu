@@ -268,6 +268,199 @@ k_interp_tma(const __grid_constant__ CUtensorMap tmap, const float2* __restrict_
     scheduler_done(sched);
 }
 
+// ---------------------------------------------------------------------
+// 1-D: every subproblem's inputs streamed through shared memory.
+//
+// A 1-D point has only W taps, so the tiled kernel's time goes to waiting
+// on its own global loads (the tile, then the sorted cells and the
+// permutation of its points) and to the scattered output stores.  Here
+// thread 0 issues, for the NEXT subproblem, 1-D bulk async copies
+// (cp.async.bulk, completion on the stage's mbarrier) of the tile (the bin
+// plus halo, contiguous in the grid), the subproblem's cells, permutation
+// and phases, while the CTA works on the current subproblem from the other
+// stage; the warps then read only shared memory and store the results.
+// Bulk copies need 16-byte-aligned ranges: each range starts at an aligned
+// element at or before its first element and is rounded up (at most 3
+// elements past the end of the point arrays, which carry that slack; see
+// kPointSlack).  Tiles that wrap around the periodic grid are loaded by
+// the CTA's threads.
+constexpr int kStreamThreads = 256;
+
+#ifndef NUFFT_STREAM_MINB
+#define NUFFT_STREAM_MINB 3
+#endif
+
+__host__ __device__ __forceinline__ int align_up(int x, int a) {
+    return (x + a - 1) / a * a;
+}
+
+// Byte offsets of one stage: [tile x nvg][cells][perm][phase]
+struct StreamLayout {
+    int tile_cells;     // per vector: T + 1 rounded up to even
+    int tile_bytes;     // per vector, 128-byte multiple
+    int cells_off, perm_off, phase_off, stage_bytes;
+};
+
+__host__ __device__ __forceinline__ StreamLayout stream_layout(int T, int msub,
+                                                              int nvg, bool phase) {
+    StreamLayout L;
+    L.tile_cells = align_up(T + 1, 2);
+    L.tile_bytes = align_up(L.tile_cells * 8, 128);
+    L.cells_off = nvg * L.tile_bytes;
+    L.perm_off = L.cells_off + align_up((msub + 2) * 8, 128);
+    L.phase_off = L.perm_off + align_up((msub + 8) * 4, 128);
+    L.stage_bytes = L.phase_off + (phase ? align_up((msub + 2) * 8, 128) : 0);
+    return L;
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+struct StreamSub {
+    int start, cnt, o;    // points [start, start + cnt), tile origin o
+    int c0, p0;           // aligned first element of the cell / perm ranges
+    int c1, p1;           // aligned ends
+    bool interior;        // tile copied by the bulk engine
+    int g0;               // aligned first grid cell of the tile copy
+};
+
+__device__ __forceinline__ StreamSub stream_sub(const int4& sb, const TileGeom& tg,
+                                                int tile_cells) {
+    StreamSub q;
+    q.start = sb.x;
+    q.cnt = sb.y;
+    q.o = (sb.z % tg.nb[0]) * tg.m[0] - tg.halfw;
+    q.g0 = q.o - (q.o & 1);
+    q.interior = q.g0 >= 0 && q.g0 + tile_cells <= tg.n[0];
+    q.c0 = q.start & ~1;
+    q.c1 = align_up(q.start + q.cnt, 2);
+    q.p0 = q.start & ~3;
+    q.p1 = align_up(q.start + q.cnt, 4);
+    return q;
+}
+
+template <int W>
+__global__ void __launch_bounds__(kStreamThreads, NUFFT_STREAM_MINB)
+k_interp1_stream(const float2* __restrict__ grid, int nvg, int msub,
+                 const uint32_t* __restrict__ perm, const int2* __restrict__ cells,
+                 const float2* __restrict__ phase, const int4* __restrict__ subs,
+                 int nsub, int* __restrict__ sched, float2* __restrict__ out,
+                 int64_t ostride, TileGeom tg, int* __restrict__ err) {
+    extern __shared__ __align__(128) unsigned char sraw[];
+    __shared__ __align__(8) uint64_t bar[2];
+    __shared__ int s_next;
+    __shared__ int s_ok;
+    const StreamLayout L = stream_layout(tg.tcells, msub, nvg, phase != nullptr);
+    const uint64_t pol = l2_evict_last_policy();
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        s_next = atomicAdd(&sched[0], 1);
+        s_ok = (smem_addr(sraw) & 127u) == 0;
+    }
+    __syncthreads();
+    if (!s_ok) {            // misaligned stage buffers: record and stop
+        if (threadIdx.x == 0) atomicOr(err, kErrTileWait);
+        scheduler_done(sched);
+        return;
+    }
+    auto stage = [&](int b) { return sraw + (size_t)b * L.stage_bytes; };
+    // thread 0: all copies of subproblem q into stage b
+    auto issue = [&](const StreamSub& q, int b) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        unsigned char* st = stage(b);
+        uint32_t bytes = (uint32_t)(q.c1 - q.c0) * 8 + (uint32_t)(q.p1 - q.p0) * 4;
+        if (phase) bytes += (uint32_t)(q.c1 - q.c0) * 8;
+        if (q.interior) bytes += (uint32_t)nvg * L.tile_cells * 8;
+        mbar_expect_tx(&bar[b], bytes);
+        if (q.interior)
+            for (int v = 0; v < nvg; ++v)
+                bulk_load(st + v * L.tile_bytes, grid + (int64_t)v * tg.ncells + q.g0,
+                          (uint32_t)L.tile_cells * 8, &bar[b]);
+        bulk_load(st + L.cells_off, cells + q.c0, (uint32_t)(q.c1 - q.c0) * 8, &bar[b]);
+        bulk_load(st + L.perm_off, perm + q.p0, (uint32_t)(q.p1 - q.p0) * 4, &bar[b]);
+        if (phase)
+            bulk_load(st + L.phase_off, phase + q.c0, (uint32_t)(q.c1 - q.c0) * 8,
+                      &bar[b]);
+    };
+    int cur = s_next;
+    int b = 0;
+    uint32_t parity0 = 0u, parity1 = 0u;
+    if (cur < nsub && threadIdx.x == 0) issue(stream_sub(subs[cur], tg, L.tile_cells), 0);
+    bool failed = false, pending_other = false;
+    while (cur < nsub) {
+        __syncthreads();                       // stage b ^ 1 and s_next free
+        if (threadIdx.x == 0) s_next = atomicAdd(&sched[0], 1);
+        __syncthreads();
+        const int nxt = s_next;
+        pending_other = nxt < nsub;
+        if (pending_other && threadIdx.x == 0)
+            issue(stream_sub(subs[nxt], tg, L.tile_cells), b ^ 1);
+        const StreamSub q = stream_sub(subs[cur], tg, L.tile_cells);
+        const bool ok = mbar_wait(&bar[b], b ? parity1 : parity0);
+        if (b) parity1 ^= 1u; else parity0 ^= 1u;
+        if (__syncthreads_or(!ok)) {
+            failed = true;
+            break;
+        }
+        unsigned char* st = stage(b);
+        const float2* tile = reinterpret_cast<const float2*>(st);
+        int xoff = q.o - q.g0;
+        if (!q.interior) {
+            float2* tw = reinterpret_cast<float2*>(st);
+            for (int c = threadIdx.x; c < tg.tcells; c += blockDim.x) {
+                const int g = wrap_tile(q.o + c, tg.n[0]);
+                for (int v = 0; v < nvg; ++v)
+                    tw[v * (L.tile_bytes / 8) + c] = grid[(int64_t)v * tg.ncells + g];
+            }
+            __syncthreads();
+            xoff = 0;
+        }
+        const int2* sc = reinterpret_cast<const int2*>(st + L.cells_off) + (q.start - q.c0);
+        const uint32_t* sp = reinterpret_cast<const uint32_t*>(st + L.perm_off) +
+                             (q.start - q.p0);
+        const float2* sh = phase ? reinterpret_cast<const float2*>(st + L.phase_off) +
+                                       (q.start - q.c0)
+                                 : nullptr;
+        for (int t = threadIdx.x; t < q.cnt; t += blockDim.x) {
+            const int2 cl = sc[t];
+            const int l0 = cl.x - q.o;
+            float wgt[W];
+            kernel_weights<W>(__int_as_float(cl.y), tg, wgt);
+            const bool inb = (unsigned)l0 < (unsigned)tg.m[0];
+            const int64_t dst = sp[t];
+            for (int v = 0; v < nvg; ++v) {
+                float2 acc = make_float2(0.0f, 0.0f);
+                if (inb) {
+                    const float2* tv = tile + v * (L.tile_bytes / 8) + l0 + xoff;
+#pragma unroll
+                    for (int a = 0; a < W; ++a) {
+                        const float2 g = tv[a];
+                        acc.x = fmaf(g.x, wgt[a], acc.x);
+                        acc.y = fmaf(g.y, wgt[a], acc.y);
+                    }
+                    if (sh) acc = cmul(acc, sh[t]);
+                }
+                st_keep(out + v * ostride + dst, acc, pol);
+            }
+        }
+        cur = nxt;
+        b ^= 1;
+    }
+    if (failed && threadIdx.x == 0) {
+        atomicOr(err, kErrTileWait);
+        if (pending_other) mbar_wait(&bar[b ^ 1], b ? parity0 : parity1);
+    }
+    scheduler_done(sched);
+}
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no
 // libcuda link); null when the driver does not provide it.
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
@@ -340,9 +533,39 @@ void interp_tma_impl(const PointSet& ps, const TileGeom& tg, const CUtensorMap& 
     }
 }
 
+template <int W>
+void interp1_stream_impl(const PointSet& ps, const TileGeom& tg, const float2* grid,
+                         int nvec, float2* out, int64_t ostride, int nvg, int msub,
+                         int* err, cudaStream_t st) {
+    auto k = k_interp1_stream<W>;
+    for (int v0 = 0; v0 < nvec; v0 += nvg) {
+        const int nv = std::min(nvg, nvec - v0);
+        const StreamLayout L = stream_layout(tg.tcells, msub, nv, ps.phase != nullptr);
+        const size_t smem = 2 * (size_t)L.stage_bytes;
+        ensure_smem((const void*)k, smem);
+        const int blocks = persistent_grid((const void*)k, smem, ps.nsub,
+                                           kStreamThreads);
+        k<<<blocks, kStreamThreads, smem, st>>>(
+            grid + (int64_t)v0 * tg.ncells, nv, msub, ps.perm, ps.cell[0], ps.phase,
+            ps.subs, (int)ps.nsub, ps.sched, out + v0 * ostride, ostride, tg, err);
+        NUFFT_LAUNCH("k_interp1_stream");
+    }
+}
+
 bool launch_interp_tma(const PointSet& ps, const TileGeom& tg, int w,
                        const CUtensorMap* map, const float2* grid, int nvec,
                        float2* out, int64_t ostride, int* err, cudaStream_t st) {
+    if (ps.tiled && ps.sorted && ps.dim == 1 && ps.msub > 0 && ps.msub <= kStreamMsubMax &&
+        w <= 16 && grid) {
+        if (ps.nsub == 0) return true;
+        // vectors per pass: two stages within ~72 KB
+        const size_t one = (size_t)stream_layout(tg.tcells, ps.msub, 1,
+                                                  ps.phase != nullptr).stage_bytes;
+        const int nvg = (int)std::max<size_t>(1, (36 * 1024) / one);
+        NUFFT_WIDTH_SWITCH(w, interp1_stream_impl<W>(ps, tg, grid, nvec, out, ostride,
+                                                     nvg, ps.msub, err, st));
+        return true;
+    }
     if (!map || !ps.tiled || ps.dim != 3 || w > 10) return false;
     if (ps.nsub == 0) return true;
     // two buffers of up to nvg vectors within ~100 KB: two CTAs per SM

@@ -160,6 +160,10 @@ struct nufft_plan_s {
 
 namespace nufft_impl {
 
+// Points per interpolation subproblem: 1-D subproblems are streamed
+// through a shared-memory stage (interp_tma.cu), at most kStreamMsubMax.
+int interp_msub(int dim) { return dim == 1 ? kStreamMsubMax : kMsubInterp; }
+
 // Integer tuning override from the environment (NUFFT_BIN_1D,
 // NUFFT_SORT_CHUNK_LOG2, NUFFT_TILE_KB); the default when unset.
 int env_int(const char* name, int dflt) {
@@ -215,12 +219,10 @@ void plane_tap_order(TileGeom& tg, int w) {
 // ----------------------------------------------------------------------
 // tiling choice per grid: bin extent m per dimension so that the tile
 // (m + w - 1)^dim of complex64 fits shared memory with room for several
-// vectors.  1-D bins are 4096 cells for interpolation (each subproblem
-// loads its tile once, so longer bins cut the number of scattered output
-// windows) and 1024 for spreading (each subproblem flushes its whole tile);
-// 32 x 32 in 2-D, 8 x 8 x 8 in 3-D.
-TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
-                   bool interp) {
+// vectors: 1024 cells in 1-D (the streamed 1-D interpolation stages a
+// subproblem's tile in shared memory next to its points), 32 x 32 in 2-D,
+// 8 x 8 x 8 in 3-D.
+TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval) {
     TileGeom tg{};
     tg.dim = dim;
     tg.ncells = 1;
@@ -231,7 +233,7 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
     tg.keval = keval ? 1 : 0;
     tg.poly = make_es_poly(w, beta);
     static const int m1d = env_int("NUFFT_BIN_1D", 0);
-    const int m1 = m1d > 0 ? m1d : (interp ? 4096 : 1024);
+    const int m1 = m1d > 0 ? m1d : 1024;
     int m0 = dim == 1 ? m1 : (dim == 2 ? 32 : 8);
     for (int d = 0; d < 3; ++d) {
         if (d < dim) {
@@ -438,8 +440,7 @@ void create_t12(nufft_plan_s* p) {
         }
         upload_dec(p, d, v);
     }
-    p->tg_src = make_tile(p->dim, p->nup, p->w, p->beta, p->opts.kerevalmeth,
-                          p->type == 2);
+    p->tg_src = make_tile(p->dim, p->nup, p->w, p->beta, p->opts.kerevalmeth);
     p->nvg_src = vectors_per_tile(p->tg_src, p->nbatch);
     alloc_grids(p);
     p->sized = true;
@@ -464,8 +465,8 @@ void setpts_t12(nufft_plan_s* p, int64_t M, const double* const* xs,
     cp.chunk = tiled ? sort_chunk(p->dim) : 0;
     PhaseParams pp{};
     build_pointset(&p->src, cp, M, xs, sort, tiled,
-                   p->type == 1 ? kMsubSpread : kMsubInterp, p->type == 2, pp,
-                   p->d_err, st);
+                   p->type == 1 ? kMsubSpread : interp_msub(p->dim), p->type == 2,
+                   pp, p->d_err, st);
     check_err_flag(p, st);
     p->points_set = true;
 }
@@ -542,11 +543,9 @@ void size_t3(nufft_plan_s* p, const double* slo, const double* shi) {
         destroy_ffts(p);
         alloc_grids(p);
     }
-    p->tg_src = make_tile(p->dim, p->nf, p->w, p->beta, p->opts.kerevalmeth,
-                          false);
+    p->tg_src = make_tile(p->dim, p->nf, p->w, p->beta, p->opts.kerevalmeth);
     p->nvg_src = vectors_per_tile(p->tg_src, p->nbatch);
-    p->tg_tgt = make_tile(p->dim, p->nup, p->w2, p->beta2, p->opts.kerevalmeth,
-                          true);
+    p->tg_tgt = make_tile(p->dim, p->nup, p->w2, p->beta2, p->opts.kerevalmeth);
     p->nvg_tgt = vectors_per_tile(p->tg_tgt, p->nbatch);
     p->sized = true;
 }
@@ -654,7 +653,7 @@ void setpts_t3(nufft_plan_s* p, int64_t M, const double* const* xs, int64_t N,
     const bool tiled = want_tiled(p, N, p->tg_tgt);
     const bool sort = tiled || p->opts.sort_points;
     cp.chunk = tiled ? sort_chunk(p->dim) : 0;
-    build_pointset(&p->tgt, cp, N, ss, sort, tiled, kMsubInterp, true, pp,
+    build_pointset(&p->tgt, cp, N, ss, sort, tiled, interp_msub(p->dim), true, pp,
                    p->d_err, st);
     check_err_flag(p, st);
     p->Ntgt = N;
@@ -678,6 +677,13 @@ const CUtensorMap* interp_tmap(nufft_plan_s* p, const TileGeom& tg) {
         for (int d = 0; d < 3; ++d) p->tmap_n[d] = tg.n[d];
     }
     return p->tmap_ok ? &p->tmap : nullptr;
+}
+
+// The complex64 FFT grid for the staged interpolation kernels (null: fp64
+// FFT grid, or the path disabled with NUFFT_INTERP_STREAM=0 for tuning).
+const float2* interp_grid32(const nufft_plan_s* p) {
+    static const int on = env_int("NUFFT_INTERP_STREAM", 1);
+    return (p->fft64 || !on) ? nullptr : p->gfft;
 }
 
 void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
@@ -724,7 +730,7 @@ void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
             record(p, 2, st);
         }
         if (!launch_interp_tma(p->src, p->tg_src, p->w, interp_tmap(p, p->tg_src),
-                               p->gfft, nv, out, p->src.M, p->d_err, st))
+                               interp_grid32(p), nv, out, p->src.M, p->d_err, st))
             launch_interp(p->src, p->tg_src, p->w, p->gfft, p->fft64, nv, out,
                           p->src.M, p->nvg_src, st);
         record(p, 3, st);
@@ -739,7 +745,7 @@ void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
         run_fft(p, nv, st);
         record(p, 2, st);
         if (!launch_interp_tma(p->tgt, p->tg_tgt, p->w2, interp_tmap(p, p->tg_tgt),
-                               p->gfft, nv, out, p->Ntgt, p->d_err, st))
+                               interp_grid32(p), nv, out, p->Ntgt, p->d_err, st))
             launch_interp(p->tgt, p->tg_tgt, p->w2, p->gfft, p->fft64, nv, out,
                           p->Ntgt, p->nvg_tgt, st);
         record(p, 3, st);

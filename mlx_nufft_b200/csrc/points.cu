@@ -424,8 +424,8 @@ void sub_sort(PointSet* ps, const CellParams& cp, int msub, cudaStream_t st) {
     uint32_t* np = nullptr;
     try {
         for (int d = 0; d < DIM; ++d)
-            nc[d] = (int2*)dmalloc(sizeof(int2) * ps->cap, "sorted cells");
-        np = (uint32_t*)dmalloc(4 * ps->cap, "sorted permutation");
+            nc[d] = (int2*)dmalloc(sizeof(int2) * (ps->cap + kPointSlack), "sorted cells");
+        np = (uint32_t*)dmalloc(4 * (ps->cap + kPointSlack), "sorted permutation");
     } catch (...) {
         for (int d = 0; d < DIM; ++d) dfree(nc[d]);
         throw;
@@ -539,15 +539,17 @@ void build_pointset(PointSet* ps, const CellParams& cp, int64_t M,
     if (M > ps->cap || (sort && !ps->perm) || (pp.mode && !ps->phase)) {
         free_pointset(ps);
         for (int d = 0; d < cp.dim; ++d)
-            ps->cell[d] = (int2*)dmalloc(sizeof(int2) * M, "point cells");
-        ps->perm = (uint32_t*)dmalloc(4 * M, "point permutation");
-        if (pp.mode) ps->phase = (float2*)dmalloc(sizeof(float2) * M, "phases");
+            ps->cell[d] = (int2*)dmalloc(sizeof(int2) * (M + kPointSlack), "point cells");
+        ps->perm = (uint32_t*)dmalloc(4 * (M + kPointSlack), "point permutation");
+        if (pp.mode)
+            ps->phase = (float2*)dmalloc(sizeof(float2) * (M + kPointSlack), "phases");
         ps->sched = (int*)dmalloc(2 * sizeof(int), "scheduler");
         NUFFT_CUDA(cudaMemsetAsync(ps->sched, 0, 2 * sizeof(int), st));
         ps->cap = M;
     }
     ps->dim = cp.dim;
     ps->M = M;
+    ps->msub = msub;
     ps->sorted = sort;
     ps->tiled = tiled && sort;
     switch (cp.dim) {

@@ -194,3 +194,20 @@ def test_expi_isign_components_shape(rng):
     # beyond the reference's ceiling the fp64 reduction stays accurate
     big = rng.uniform(-1e9, 1e9, 50_000)
     assert np.max(np.abs(expi(big, return_np=True) - np.exp(1j * big))) < 1e-5
+
+
+def test_type3_1d_tiled_targets(rng):
+    """1-D type 3 with enough targets for the tiled (streamed) interp, whose
+    stages carry the targets' post-phases."""
+    from mlx_nufft_b200 import Type3Plan
+    P, M = 30_000, 60_000
+    x = [rng.uniform(-8, 8, P)]
+    s = [rng.uniform(-40, 40, M)]
+    c = rng.standard_normal(P) + 1j * rng.standard_normal(P)
+    plan = Type3Plan(tuple(x), tuple(s), eps=1e-5)
+    assert plan._plan.info().nsub_tgt > 0
+    f = plan.execute(c)
+    idx = rng.choice(M, 400, replace=False)
+    exact = fast.direct_sum(x, c, s, +1, idx)
+    floor = port.rel_l2(port.nufft_t3_fp32(x, c, s, eps=1e-5, isign=+1)[idx], exact)
+    assert port.rel_l2(f[idx], exact) <= max(gate(1e-5), REF32_SLACK * floor)
