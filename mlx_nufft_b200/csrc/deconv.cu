@@ -5,11 +5,11 @@
 // pad (type 2 nd.py:878-906, type 3 gpu_t3.py:629-651): mode box times the
 //   correction into the zero-padded FFT-ordered fine grid (zeros written too,
 //   so no separate memset pass).
-// Both run one CTA row per outer-index row of the output and sweep the
-// innermost (contiguous) dimension with consecutive threads, so every global
-// access is coalesced and index decomposition costs two integer divisions
-// per CTA rather than per element.  The outer-dimension correction factor
-// is formed once per row.
+// Both sweep the innermost (contiguous) dimension with consecutive threads,
+// so every global access is coalesced; a CTA covers part of one long row or
+// several whole short rows (RowSplit), so thin innermost dimensions do not
+// leave most threads idle.  The outer-dimension correction factor is formed
+// once per row.
 //
 // expi (mlx_nufft/dfmath.py:29-134): the reference forms the phase in
 // double-single and reduces it mod 2 pi before fp32 cos/sin.  B200 has
@@ -54,15 +54,37 @@ __device__ __forceinline__ float2 to_f2(double2 v) {
     return make_float2((float)v.x, (float)v.y);
 }
 
+// Work split shared by crop and pad: a CTA covers `chunks` blocks of 256
+// consecutive innermost elements of one row, or, when a row is shorter than
+// the CTA, `rows` whole rows (so short innermost dimensions -- a thin axis
+// of a type-3 grid -- still fill the CTA).  Element e of row `row`:
+struct RowSplit {
+    int per_row;     // elements (or element pairs) per row
+    int rows;        // rows per CTA (>= 1)
+    int chunks;      // CTAs per row (>= 1)
+};
+
+__device__ __forceinline__ bool row_elem(const RowSplit& rs, int64_t* row, int* e) {
+    if (rs.rows > 1) {
+        const int lr = (int)threadIdx.x / rs.per_row;
+        *row = (int64_t)blockIdx.x * rs.rows + lr;
+        *e = (int)threadIdx.x - lr * rs.per_row;
+        return lr < rs.rows;
+    }
+    *row = blockIdx.x / rs.chunks;
+    *e = (int)(blockIdx.x % rs.chunks) * blockDim.x + threadIdx.x;
+    return *e < rs.per_row;
+}
+
 template <typename G>
 __global__ void __launch_bounds__(256)
 k_crop(const G* __restrict__ grid, float2* __restrict__ fk, DecPtrs dec,
-       BoxGrid bg, int chunks_per_row) {
+       BoxGrid bg, RowSplit rs, int64_t nrows) {
     const int dim = bg.dim;
     const int L = dim - 1;                    // innermost dim index
-    const int64_t row = blockIdx.x / chunks_per_row;
-    const int m_in = (int)(blockIdx.x % chunks_per_row) * blockDim.x + threadIdx.x;
-    if (m_in >= bg.N[L]) return;
+    int64_t row;
+    int m_in;
+    if (!row_elem(rs, &row, &m_in) || row >= nrows) return;
     const int v = blockIdx.y;
     int m[3] = {0, 0, 0};
     split_row(row, bg.N, dim, m);
@@ -106,12 +128,13 @@ __device__ __forceinline__ void store_pair(double2* p, float4 v) {
 template <typename H_T>
 __global__ void __launch_bounds__(256)
 k_pad(const float2* __restrict__ f, H_T* __restrict__ H, DecPtrs dec,
-      BoxGrid bg, int chunks_per_row) {
+      BoxGrid bg, RowSplit rs, int64_t nrows) {
     const int dim = bg.dim;
     const int L = dim - 1;
-    const int64_t row = blockIdx.x / chunks_per_row;
-    const int r0 = 2 * ((int)(blockIdx.x % chunks_per_row) * blockDim.x + threadIdx.x);
-    if (r0 >= bg.n[L]) return;
+    int64_t row;
+    int pair;
+    if (!row_elem(rs, &row, &pair) || row >= nrows) return;
+    const int r0 = 2 * pair;
     const int v = blockIdx.y;
     int r[3] = {0, 0, 0};
     split_row(row, bg.n, dim, r);
@@ -167,6 +190,22 @@ BoxGrid make_boxgrid(int dim, const int64_t* N, const int64_t* n) {
     return bg;
 }
 
+// CTAs and work split for rows of `per_row` elements (256 threads).
+RowSplit make_split(int per_row, int64_t nrows, int64_t* blocks) {
+    RowSplit rs{};
+    rs.per_row = per_row;
+    if (per_row <= 128) {
+        rs.rows = 256 / per_row;
+        rs.chunks = 1;
+        *blocks = (nrows + rs.rows - 1) / rs.rows;
+    } else {
+        rs.rows = 1;
+        rs.chunks = (per_row + 255) / 256;
+        *blocks = nrows * rs.chunks;
+    }
+    return rs;
+}
+
 DecPtrs make_dec(const float* const* dec) {
     DecPtrs dp{};
     for (int d = 0; d < 3; ++d) dp.d[d] = dec[d];
@@ -180,19 +219,19 @@ void launch_crop(int dim, const int64_t* N, const int64_t* n,
                  float2* fk, int nvec, cudaStream_t st) {
     const BoxGrid bg = make_boxgrid(dim, N, n);
     const int inner = bg.N[dim - 1];
-    const int cpr = (inner + 255) / 256;
     const int64_t rows = bg.K / inner;
-    const int64_t blocks = rows * cpr;
+    int64_t blocks = 0;
+    const RowSplit rs = make_split(inner, rows, &blocks);
     if (blocks > 0x7fffffffLL) fail(-1, "mode box too large");
     for (int v0 = 0; v0 < nvec; v0 += 65535) {
         const int nv = std::min(65535, nvec - v0);
         dim3 g((unsigned)blocks, (unsigned)nv);
         if (grid64)
             k_crop<<<g, 256, 0, st>>>((const double2*)grid + v0 * bg.ncells,
-                                      fk + v0 * bg.K, make_dec(dec), bg, cpr);
+                                      fk + v0 * bg.K, make_dec(dec), bg, rs, rows);
         else
             k_crop<<<g, 256, 0, st>>>((const float2*)grid + v0 * bg.ncells,
-                                      fk + v0 * bg.K, make_dec(dec), bg, cpr);
+                                      fk + v0 * bg.K, make_dec(dec), bg, rs, rows);
         NUFFT_LAUNCH("k_crop");
     }
 }
@@ -203,19 +242,19 @@ void launch_pad(int dim, const int64_t* N, const int64_t* n,
     const BoxGrid bg = make_boxgrid(dim, N, n);
     const int inner = bg.n[dim - 1];
     if (inner % 2) fail(-1, "fine-grid extents must be even");
-    const int cpr = (inner / 2 + 255) / 256;
     const int64_t rows = bg.ncells / inner;
-    const int64_t blocks = rows * cpr;
+    int64_t blocks = 0;
+    const RowSplit rs = make_split(inner / 2, rows, &blocks);
     if (blocks > 0x7fffffffLL) fail(-1, "fine grid too large");
     for (int v0 = 0; v0 < nvec; v0 += 65535) {
         const int nv = std::min(65535, nvec - v0);
         dim3 g((unsigned)blocks, (unsigned)nv);
         if (grid64)
             k_pad<<<g, 256, 0, st>>>(f + v0 * bg.K, (double2*)H + v0 * bg.ncells,
-                                     make_dec(dec), bg, cpr);
+                                     make_dec(dec), bg, rs, rows);
         else
             k_pad<<<g, 256, 0, st>>>(f + v0 * bg.K, (float2*)H + v0 * bg.ncells,
-                                     make_dec(dec), bg, cpr);
+                                     make_dec(dec), bg, rs, rows);
         NUFFT_LAUNCH("k_pad");
     }
 }

@@ -538,14 +538,14 @@ void interp1_stream_impl(const PointSet& ps, const TileGeom& tg, const float2* g
                          int nvec, float2* out, int64_t ostride, int nvg, int msub,
                          int* err, cudaStream_t st) {
     auto k = k_interp1_stream<W>;
+    const int threads = kStreamThreads, stages = 2;
     for (int v0 = 0; v0 < nvec; v0 += nvg) {
         const int nv = std::min(nvg, nvec - v0);
         const StreamLayout L = stream_layout(tg.tcells, msub, nv, ps.phase != nullptr);
-        const size_t smem = 2 * (size_t)L.stage_bytes;
+        const size_t smem = stages * (size_t)L.stage_bytes;
         ensure_smem((const void*)k, smem);
-        const int blocks = persistent_grid((const void*)k, smem, ps.nsub,
-                                           kStreamThreads);
-        k<<<blocks, kStreamThreads, smem, st>>>(
+        const int blocks = persistent_grid((const void*)k, smem, ps.nsub, threads);
+        k<<<blocks, threads, smem, st>>>(
             grid + (int64_t)v0 * tg.ncells, nv, msub, ps.perm, ps.cell[0], ps.phase,
             ps.subs, (int)ps.nsub, ps.sched, out + v0 * ostride, ostride, tg, err);
         NUFFT_LAUNCH("k_interp1_stream");

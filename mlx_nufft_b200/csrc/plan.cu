@@ -103,6 +103,7 @@ std::mutex g_plan_mutex;   // serialises plan creation / cuFFT planning
 constexpr int kMsubSpread = 1024;   // points per spreading subproblem
 constexpr int kMsubInterp = 8192;   // points per interpolation subproblem
 constexpr int64_t kTiledMinPoints = 20000;  // below: global kernels (nd.py:304)
+constexpr int kTiledMinPerBin = 8;          // points per bin, see want_tiled
 constexpr size_t kTileBudget = 96 * 1024;   // smem per CTA for vector groups
 
 }  // namespace
@@ -286,6 +287,10 @@ int vectors_per_tile(const TileGeom& tg, int nbatch) {
     return std::max(1, std::min(nvg, nbatch));
 }
 
+// Automatic choice: tiled when the tile fits, there are enough points
+// (nd.py:304), and the points per bin on average pay for the per-subproblem
+// tile traffic (one load, or one zero + flush, of the whole tile).  Below
+// that density the global kernels touch only the points' own taps.
 bool want_tiled(const nufft_plan_s* p, int64_t npts, const TileGeom& tg) {
     if (p->opts.method == NUFFT_METHOD_GLOBAL) return false;
     const bool fits = tile_fits(tg);
@@ -293,7 +298,10 @@ bool want_tiled(const nufft_plan_s* p, int64_t npts, const TileGeom& tg) {
         if (!fits) fail(NUFFT_ERR_ARG, "tiled method not applicable: tile exceeds shared memory");
         return true;
     }
-    return fits && npts >= kTiledMinPoints;
+    static const int min_per_bin = env_int("NUFFT_MIN_PER_BIN", kTiledMinPerBin);
+    double bins = 1.0;
+    for (int d = 0; d < tg.dim; ++d) bins *= tg.nb[d];
+    return fits && npts >= kTiledMinPoints && (double)npts >= min_per_bin * bins;
 }
 
 void upload_dec(nufft_plan_s* p, int d, const std::vector<double>& v) {

@@ -99,15 +99,22 @@ void spread_impl(const PointSet& ps, const TileGeom& tg, const float2* c,
     if (ps.tiled) {
         if (ps.nsub == 0) return;
         if constexpr (DIM == 3 && W <= 10) {
-            // groups of 4, 2 or 1 vectors, each group's tile within 96 KB
+            // groups of 8, 4, 2 or 1 vectors, each group's tile within the
+            // budget (NUFFT_PLANE_KB overrides it, tuning)
+            static const size_t budget = [] {
+                const char* e = std::getenv("NUFFT_PLANE_KB");
+                return (e && *e) ? (size_t)std::atoi(e) * 1024 : kPlaneTileBudget;
+            }();
             const size_t per = (size_t)tg.T[0] * tg.T[1] * tg.S2 * sizeof(float2);
             for (int v0 = 0; v0 < nvec;) {
                 const int left = nvec - v0;
-                const int nv = (left >= 4 && 4 * per <= kPlaneTileBudget) ? 4
-                             : (left >= 2 && 2 * per <= kPlaneTileBudget) ? 2 : 1;
+                const int nv = (left >= 8 && 8 * per <= budget) ? 8
+                             : (left >= 4 && 4 * per <= budget) ? 4
+                             : (left >= 2 && 2 * per <= budget) ? 2 : 1;
                 const float2* cv = c + v0 * cstride;
                 float2* gv = grid + v0 * tg.ncells;
-                if (nv == 4) launch_planes<W, 4>(ps, tg, cv, cstride, perm, cells, gv, st);
+                if (nv == 8) launch_planes<W, 8>(ps, tg, cv, cstride, perm, cells, gv, st);
+                else if (nv == 4) launch_planes<W, 4>(ps, tg, cv, cstride, perm, cells, gv, st);
                 else if (nv == 2) launch_planes<W, 2>(ps, tg, cv, cstride, perm, cells, gv, st);
                 else launch_planes<W, 1>(ps, tg, cv, cstride, perm, cells, gv, st);
                 v0 += nv;

@@ -83,7 +83,8 @@ CONFIG_NAMES = {
 
 
 def config(k, scale=1.0, seed=0):
-    """BASELINE workload k (1..5; 6 = the standalone expi of cfg 5).
+    """BASELINE workload k (1..5; 6 = the standalone expi of cfg 5; 7..12 =
+    the reference's type-3 paper suite, PAPER_T3).
 
     Returns a dict with keys: type, dim, eps, isign, x (list of fp64
     coordinate arrays), data (strengths or modes), and n_modes / s / phi as
@@ -136,4 +137,21 @@ def config(k, scale=1.0, seed=0):
         n = m(10_000_000)
         return dict(type=0, phi=rng.uniform(-1e6, 1e6, n), isign=+1,
                     name=CONFIG_NAMES[6])
+    if k in PAPER_T3:
+        # the reference's type-3 acceptance / paper suite, 1e6 sources
+        # (harness/run_acceptance.py:25-41, 99-128; mlx-nufft.pdf Table I)
+        geom, N = PAPER_T3[k]
+        P = m(1_000_000)
+        prob = (gen_generic(N=N, P=P, seed=seed) if geom == "generic"
+                else gen_anisotropic(N=N, P=P, lat=1.5, seed=seed))
+        return dict(type=3, dim=3, eps=3e-5 if geom == "generic" else 1e-5,
+                    isign=+1, x=list(prob["x"]), data=prob["c"],
+                    s=list(prob["s"]),
+                    name=f"3D type-3 {geom} N={N} ({N * N} targets) P=1e6")
     raise ValueError(f"unknown config {k}")
+
+
+# bench configs 7..12: (geometry, N) of the reference's type-3 paper suite
+PAPER_T3 = {7: ("generic", 512), 8: ("generic", 1024), 9: ("generic", 2048),
+            10: ("anisotropic", 512), 11: ("anisotropic", 1024),
+            12: ("anisotropic", 2048)}

@@ -211,3 +211,21 @@ def test_type3_1d_tiled_targets(rng):
     exact = fast.direct_sum(x, c, s, +1, idx)
     floor = port.rel_l2(port.nufft_t3_fp32(x, c, s, eps=1e-5, isign=+1)[idx], exact)
     assert port.rel_l2(f[idx], exact) <= max(gate(1e-5), REF32_SLACK * floor)
+
+
+@pytest.mark.parametrize("geom", ["generic", "anisotropic"])
+def test_type3_paper_geometries(geom, rng):
+    """The reference's acceptance geometries (harness/run_acceptance.py:
+    generic at eps 3e-5, anisotropic -- source axes ~1e7, targets ~1e-4, a
+    thin third axis -- at eps 1e-5), reduced in size, against the exact sum
+    within 1.5x of the reference's fp32 pipeline on the same inputs."""
+    from mlx_nufft_b200 import Type3Plan, gen
+    prob = (gen.gen_generic(N=96, P=20_000, seed=3) if geom == "generic"
+            else gen.gen_anisotropic(N=96, P=20_000, lat=1.5, seed=3))
+    eps = 3e-5 if geom == "generic" else 1e-5
+    x, c, s = list(prob["x"]), prob["c"], list(prob["s"])
+    f = Type3Plan(tuple(x), tuple(s), eps=eps, isign=+1).execute(c)
+    idx = rng.choice(s[0].size, 600, replace=False)
+    exact = fast.direct_sum(x, c, s, +1, idx)
+    floor = port.rel_l2(port.nufft_t3_fp32(x, c, s, eps=eps, isign=+1)[idx], exact)
+    assert port.rel_l2(f[idx], exact) <= max(gate(eps), REF32_SLACK * floor)
