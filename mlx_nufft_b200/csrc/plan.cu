@@ -222,8 +222,11 @@ void plane_tap_order(TileGeom& tg, int w) {
 // (m + w - 1)^dim of complex64 fits shared memory with room for several
 // vectors: 1024 cells in 1-D (the streamed 1-D interpolation stages a
 // subproblem's tile in shared memory next to its points), 32 x 32 in 2-D,
-// 8 x 8 x 8 in 3-D.
-TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval) {
+// 8 x 8 x 8 in 3-D for spreading (room for several vectors' tiles) and
+// 10 x 10 x 10 for 3-D interpolation (more points per subproblem, less halo:
+// measured 21-27 % faster than 8^3 on the 3-D BASELINE configs).
+TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
+                   bool interp) {
     TileGeom tg{};
     tg.dim = dim;
     tg.ncells = 1;
@@ -235,7 +238,9 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval) {
     tg.poly = make_es_poly(w, beta);
     static const int m1d = env_int("NUFFT_BIN_1D", 0);
     const int m1 = m1d > 0 ? m1d : 1024;
-    int m0 = dim == 1 ? m1 : (dim == 2 ? 32 : 8);
+    static const int m3i = env_int("NUFFT_BIN_3D_INTERP", 0);
+    const int m3 = interp ? (m3i > 0 ? m3i : 10) : 8;
+    int m0 = dim == 1 ? m1 : (dim == 2 ? 32 : m3);
     for (int d = 0; d < 3; ++d) {
         if (d < dim) {
             tg.n[d] = (int)n[d];
@@ -448,7 +453,8 @@ void create_t12(nufft_plan_s* p) {
         }
         upload_dec(p, d, v);
     }
-    p->tg_src = make_tile(p->dim, p->nup, p->w, p->beta, p->opts.kerevalmeth);
+    p->tg_src = make_tile(p->dim, p->nup, p->w, p->beta, p->opts.kerevalmeth,
+                          p->type == 2);
     p->nvg_src = vectors_per_tile(p->tg_src, p->nbatch);
     alloc_grids(p);
     p->sized = true;
@@ -551,9 +557,11 @@ void size_t3(nufft_plan_s* p, const double* slo, const double* shi) {
         destroy_ffts(p);
         alloc_grids(p);
     }
-    p->tg_src = make_tile(p->dim, p->nf, p->w, p->beta, p->opts.kerevalmeth);
+    p->tg_src = make_tile(p->dim, p->nf, p->w, p->beta, p->opts.kerevalmeth,
+                          false);
     p->nvg_src = vectors_per_tile(p->tg_src, p->nbatch);
-    p->tg_tgt = make_tile(p->dim, p->nup, p->w2, p->beta2, p->opts.kerevalmeth);
+    p->tg_tgt = make_tile(p->dim, p->nup, p->w2, p->beta2, p->opts.kerevalmeth,
+                          true);
     p->nvg_tgt = vectors_per_tile(p->tg_tgt, p->nbatch);
     p->sized = true;
 }
