@@ -140,6 +140,13 @@ struct PointSet {
     int* sched = nullptr;       // 2 ints: dynamic subproblem scheduler state
     bool sorted = false;
     bool tiled = false;
+    // kept across setpts calls (re-pointing allocates nothing once sized):
+    // sort scratch, and the second cell / permutation buffers of the
+    // per-subproblem cell-order pass
+    void* scratch = nullptr;
+    size_t scratch_bytes = 0;
+    int2* cell_alt[3] = {nullptr, nullptr, nullptr};
+    uint32_t* perm_alt = nullptr;
 };
 
 // CTAs for a persistent launch of `kernel` (256 threads, `smem` bytes):

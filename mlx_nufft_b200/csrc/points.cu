@@ -12,6 +12,7 @@
 // each point's rank inside its bin, an exclusive scan of the bin counts,
 // and a scatter -- O(M) with two coalesced reads of the coordinates.
 #include <algorithm>
+#include <utility>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -394,6 +395,15 @@ void free_pointset(PointSet* ps) {
     dfree(ps->subs);
     dfree(ps->phase);
     dfree(ps->sched);
+    dfree(ps->scratch);
+    for (int d = 0; d < 3; ++d) {
+        dfree(ps->cell_alt[d]);
+        ps->cell_alt[d] = nullptr;
+    }
+    dfree(ps->perm_alt);
+    ps->scratch = nullptr;
+    ps->scratch_bytes = 0;
+    ps->perm_alt = nullptr;
     ps->perm = nullptr;
     ps->subs = nullptr;
     ps->phase = nullptr;
@@ -420,33 +430,19 @@ void sub_sort(PointSet* ps, const CellParams& cp, int msub, cudaStream_t st) {
                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)smem));
     }
-    int2* nc[3] = {nullptr, nullptr, nullptr};
-    uint32_t* np = nullptr;
-    try {
+    // second buffers, kept in the point set and swapped with the primary ones
+    if (!ps->perm_alt) {
         for (int d = 0; d < DIM; ++d)
-            nc[d] = (int2*)dmalloc(sizeof(int2) * (ps->cap + kPointSlack), "sorted cells");
-        np = (uint32_t*)dmalloc(4 * (ps->cap + kPointSlack), "sorted permutation");
-    } catch (...) {
-        for (int d = 0; d < DIM; ++d) dfree(nc[d]);
-        throw;
+            ps->cell_alt[d] = (int2*)dmalloc(sizeof(int2) * (ps->cap + kPointSlack),
+                                             "sorted cells");
+        ps->perm_alt = (uint32_t*)dmalloc(4 * (ps->cap + kPointSlack), "sorted permutation");
     }
-    try {
-        k_sub_sort<DIM><<<(unsigned)ps->nsub, 256, smem, st>>>(
-            ps->subs, cp, mcells, ps->cell[0], ps->cell[1], ps->cell[2],
-            ps->perm, nc[0], nc[1], nc[2], np);
-        NUFFT_LAUNCH("k_sub_sort");
-        NUFFT_CUDA(cudaStreamSynchronize(st));
-    } catch (...) {
-        for (int d = 0; d < DIM; ++d) dfree(nc[d]);
-        dfree(np);
-        throw;
-    }
-    for (int d = 0; d < DIM; ++d) {
-        dfree(ps->cell[d]);
-        ps->cell[d] = nc[d];
-    }
-    dfree(ps->perm);
-    ps->perm = np;
+    k_sub_sort<DIM><<<(unsigned)ps->nsub, 256, smem, st>>>(
+        ps->subs, cp, mcells, ps->cell[0], ps->cell[1], ps->cell[2], ps->perm,
+        ps->cell_alt[0], ps->cell_alt[1], ps->cell_alt[2], ps->perm_alt);
+    NUFFT_LAUNCH("k_sub_sort");
+    for (int d = 0; d < DIM; ++d) std::swap(ps->cell[d], ps->cell_alt[d]);
+    std::swap(ps->perm, ps->perm_alt);
 }
 
 template <int DIM>
@@ -468,11 +464,26 @@ void build_impl(PointSet* ps, const CellParams& cp, int64_t M,
         const int64_t nchunks = cp.chunk ? (M + cp.chunk - 1) / cp.chunk : 1;
         const int64_t nbins = nbins_sp * nchunks;
         if (nbins > (int64_t)0x7fffffffLL) fail(-1, "too many bins");
-        uint32_t* key_of = (uint32_t*)dmalloc(4 * M, "sort keys");
-        uint32_t* rank_of = (uint32_t*)dmalloc(4 * M, "sort ranks");
-        uint32_t* count = (uint32_t*)dmalloc(4 * (nbins + 1), "bin counts");
-        uint32_t* start = (uint32_t*)dmalloc(4 * (nbins + 1), "bin starts");
-        uint32_t* tot = (uint32_t*)dmalloc(8, "scan total");
+        // sort scratch: keys and ranks per point, four arrays per sort key,
+        // the scan total; one allocation kept in the point set
+        auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
+        const size_t pb = al(4 * (size_t)M), kb = al(4 * (size_t)(nbins + 1));
+        const size_t need = 2 * pb + 4 * kb + 256;
+        if (need > ps->scratch_bytes) {
+            dfree(ps->scratch);       // previous setpts synchronised its stream
+            ps->scratch = nullptr;
+            ps->scratch_bytes = 0;
+            ps->scratch = dmalloc(need + need / 4, "sort scratch");
+            ps->scratch_bytes = need + need / 4;
+        }
+        char* sp = (char*)ps->scratch;
+        uint32_t* key_of = (uint32_t*)sp;
+        uint32_t* rank_of = (uint32_t*)(sp + pb);
+        uint32_t* count = (uint32_t*)(sp + 2 * pb);
+        uint32_t* start = (uint32_t*)(sp + 2 * pb + kb);
+        uint32_t* nsubs = (uint32_t*)(sp + 2 * pb + 2 * kb);
+        uint32_t* subofs = (uint32_t*)(sp + 2 * pb + 3 * kb);
+        uint32_t* tot = (uint32_t*)(sp + 2 * pb + 4 * kb);
         NUFFT_CUDA(cudaMemsetAsync(count, 0, 4 * (nbins + 1), st));
         k_bin_count<DIM><<<(unsigned)grid, bs, 0, st>>>(M, X, cp, key_of,
                                                        rank_of, count, d_err);
@@ -485,8 +496,6 @@ void build_impl(PointSet* ps, const CellParams& cp, int64_t M,
         NUFFT_LAUNCH("k_bin_scatter");
         ps->nsub = 0;
         if (tiled) {
-            uint32_t* nsubs = (uint32_t*)dmalloc(4 * (nbins + 1), "nsubs");
-            uint32_t* subofs = (uint32_t*)dmalloc(4 * (nbins + 1), "subofs");
             const unsigned gb = (unsigned)((nbins + 255) / 256);
             k_sub_count<<<gb, 256, 0, st>>>(count, nbins, msub, nsubs);
             NUFFT_LAUNCH("k_sub_count");
@@ -507,18 +516,10 @@ void build_impl(PointSet* ps, const CellParams& cp, int64_t M,
                                            nbins_sp, msub, ps->subs);
             NUFFT_LAUNCH("k_sub_fill");
             ps->nsub = h_tot;
-            NUFFT_CUDA(cudaStreamSynchronize(st));
-            dfree(nsubs);
-            dfree(subofs);
             if (h_tot > 0 && cell_order && DIM == 3)
                 sub_sort<DIM>(ps, cp, msub, st);
         }
-        NUFFT_CUDA(cudaStreamSynchronize(st));
-        dfree(key_of);
-        dfree(rank_of);
-        dfree(count);
-        dfree(start);
-        dfree(tot);
+        NUFFT_CUDA(cudaStreamSynchronize(st));   // scratch free for reuse
     }
     if (pp.mode) {
         k_phase<DIM><<<(unsigned)grid, bs, 0, st>>>(
