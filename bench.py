@@ -307,6 +307,86 @@ def run_reference(args, budget_s=150.0):
     print(json.dumps(line), flush=True)
 
 
+def run_expi(args, cfg, torch, dist, world, rank, local, barrier):
+    """--config 6: the standalone expi of BASELINE cfg 5 (1e7 fp64 phases
+    in [-1e6, 1e6]); metric elements/s.  Device time: CUDA events around
+    the C-ABI call on resident data; e2e: dfmath.expi from pinned host
+    phases to a host result."""
+    import ctypes
+    from mlx_nufft_b200 import expi
+    from mlx_nufft_b200._lib import check, lib
+    dev = torch.device("cuda", local)
+    phi_h = torch.from_numpy(np.ascontiguousarray(cfg["phi"])).pin_memory()
+    phi = phi_h.to(dev)
+    n = phi.numel()
+    out = torch.empty(n, dtype=torch.complex64, device=dev)
+    ptrs = (ctypes.c_void_p * 1)(phi.data_ptr())
+    flush = torch.empty(256 * 2 ** 20, dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream
+
+    def step():
+        check(lib.nufft_expi(1, ptrs, n, int(cfg["isign"]), out.data_ptr(), st))
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    sampler = ClockSampler(local)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    sampler.start()
+    for i in range(args.steps):
+        flush.zero_()
+        flush.view(torch.int64).sum()
+        ev[i][0].record()
+        step()
+        ev[i][1].record()
+    barrier()
+    clocks = sampler.stop()
+    ms = sum(a.elapsed_time(b) for a, b in ev)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    tmax = float(t.item())
+    value = world * n * args.steps / (tmax / 1e3)
+    e2e = []
+    for i in range(max(3, min(args.steps, 20)) + 2):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        expi(phi_h, isign=int(cfg["isign"]), return_np=True)
+        b.record()
+        torch.cuda.synchronize()
+        if i >= 2:
+            e2e.append(a.elapsed_time(b))
+    e2e_t = torch.tensor([float(np.median(e2e))], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    peak, peak_kind = peaks()
+    kern_ms = tmax / args.steps
+    alg = 16 * n
+    if rank == 0:
+        print(json.dumps({
+            "metric": "expi elements/sec per GPU (device-timed)", "value": value,
+            "unit": "elem/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": kern_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f64", "data": "synthetic",
+            "config": {"workload": cfg["name"], "config": args.config,
+                       "elements_per_rank": n,
+                       "l2": "flushed between steps (256 MiB write, then read)"},
+            "roofline": {"bound": "hbm", "achieved": alg / (kern_ms / 1e3) / 1e9,
+                         "peak": peak, "unit": "GB/s",
+                         "frac": alg / (kern_ms / 1e3) / 1e9 / peak,
+                         "traffic": None, "kernel": "k_expi",
+                         "algorithmic_bytes": alg, "peak_kind": peak_kind},
+            "e2e": {"value": world * n / (float(e2e_t.item()) / 1e3), "unit": "elem/s",
+                    "h2d_bytes_per_step": 8 * n, "d2h_bytes_per_step": 8 * n,
+                    "ms_per_step": float(e2e_t.item())},
+            "gpu_launches": args.steps, "clocks": clocks, "cpu_baseline": None,
+        }), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -332,6 +412,12 @@ def main():
     from mlx_nufft_b200 import gen
     # weak scaling: every rank owns its own point set (seed = rank)
     cfg = gen.config(args.config, scale=args.scale, seed=rank)
+    if cfg["type"] == 0:
+        run_expi(args, cfg, torch, dist, world, rank, local, barrier)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     plan = build_plan(cfg, torch)
     native = plan._plan
     info = native.info()
