@@ -123,7 +123,7 @@ struct TileGeom {
 constexpr int64_t kPointSlack = 16;
 // Largest subproblem (points) of the 1-D streamed interpolation, whose
 // shared-memory stage holds a subproblem's cells and permutation.
-constexpr int kStreamMsubMax = 2048;
+constexpr int kStreamMsubMax = 1024;
 
 // One sorted (or caller-ordered) set of nonuniform points on the device.
 struct PointSet {
@@ -174,10 +174,10 @@ struct PhaseParams {
     const double* fta;   // device: 128 weights a_q (post)
     int nq;
 };
-// cell_order: also order the points of each subproblem by cell (3-D
-// interpolation point sets only; measured slower for spreading, whose
-// shared atomics then collide, and for 1-D / 2-D interpolation, whose
-// scattered output stores lose their rough caller order).
+// cell_order: also order the points of each subproblem by cell
+// (interpolation point sets in 1-D and 3-D: fewer bank conflicts in the tile
+// gathers; measured slower for spreading, whose shared atomics then
+// collide, and for the 2-D interpolation).
 void build_pointset(PointSet* ps, const CellParams& cp, int64_t M,
                     const double* const* coords, bool sort, bool tiled,
                     int msub, bool cell_order, const PhaseParams& pp,

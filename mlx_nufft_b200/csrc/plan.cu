@@ -161,15 +161,19 @@ struct nufft_plan_s {
 
 namespace nufft_impl {
 
-// Points per interpolation subproblem: 1-D subproblems are streamed
-// through a shared-memory stage (interp_tma.cu), at most kStreamMsubMax.
-int interp_msub(int dim) { return dim == 1 ? kStreamMsubMax : kMsubInterp; }
-
 // Integer tuning override from the environment (NUFFT_BIN_1D,
 // NUFFT_SORT_CHUNK_LOG2, NUFFT_TILE_KB); the default when unset.
 int env_int(const char* name, int dflt) {
     const char* v = std::getenv(name);
     return (v && *v) ? std::atoi(v) : dflt;
+}
+
+// Points per interpolation subproblem: 1-D subproblems are streamed
+// through a shared-memory stage (interp_tma.cu), at most kStreamMsubMax.
+int interp_msub(int dim) {
+    static const int m1 = env_int("NUFFT_MSUB_1D", 0);   // tuning override
+    return dim == 1 ? (m1 > 0 ? std::min(m1, kStreamMsubMax) : kStreamMsubMax)
+                    : kMsubInterp;
 }
 
 // ----------------------------------------------------------------------
@@ -220,8 +224,9 @@ void plane_tap_order(TileGeom& tg, int w) {
 // ----------------------------------------------------------------------
 // tiling choice per grid: bin extent m per dimension so that the tile
 // (m + w - 1)^dim of complex64 fits shared memory with room for several
-// vectors: 1024 cells in 1-D (the streamed 1-D interpolation stages a
-// subproblem's tile in shared memory next to its points), 32 x 32 in 2-D,
+// vectors: 1024 cells in 1-D for spreading and 512 for interpolation (the
+// streamed 1-D interpolation stages a subproblem's tile in shared memory
+// next to its points; smaller stages leave room for more CTAs), 32 x 32 in 2-D,
 // 8 x 8 x 8 in 3-D for spreading (room for several vectors' tiles) and
 // 10 x 10 x 10 for 3-D interpolation (more points per subproblem, less halo:
 // measured 21-27 % faster than 8^3 on the 3-D BASELINE configs).
@@ -237,7 +242,7 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
     tg.keval = keval ? 1 : 0;
     tg.poly = make_es_poly(w, beta);
     static const int m1d = env_int("NUFFT_BIN_1D", 0);
-    const int m1 = m1d > 0 ? m1d : 1024;
+    const int m1 = m1d > 0 ? m1d : (interp ? 512 : 1024);
     static const int m3i = env_int("NUFFT_BIN_3D_INTERP", 0);
     const int m3 = interp ? (m3i > 0 ? m3i : 10) : 8;
     int m0 = dim == 1 ? m1 : (dim == 2 ? 32 : m3);

@@ -516,7 +516,7 @@ void build_impl(PointSet* ps, const CellParams& cp, int64_t M,
                                            nbins_sp, msub, ps->subs);
             NUFFT_LAUNCH("k_sub_fill");
             ps->nsub = h_tot;
-            if (h_tot > 0 && cell_order && DIM == 3)
+            if (h_tot > 0 && cell_order && DIM != 2)
                 sub_sort<DIM>(ps, cp, msub, st);
         }
         NUFFT_CUDA(cudaStreamSynchronize(st));   // scratch free for reuse
