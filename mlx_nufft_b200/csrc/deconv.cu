@@ -21,6 +21,7 @@
 #include <algorithm>
 
 #include "internal.h"
+#include "spreadinterp.cuh"   // NUFFT_DIM_SWITCH
 
 namespace nufft {
 
@@ -38,12 +39,17 @@ struct BoxGrid {
 };
 
 // Map an "outer" row index (all dims but the last) to per-dim indices.
-__device__ __forceinline__ void split_row(int64_t row, const int* ext, int dim,
-                                          int* idx) {
-    // dims 0 .. dim-2 are outer
-    for (int d = dim - 2; d >= 0; --d) {
-        idx[d] = (int)(row % ext[d]);
-        row /= ext[d];
+// Kernels are templated on DIM so that every index is a compile-time
+// constant (a runtime dimension count put these arrays, and the parameter
+// structs they index, in local memory).
+template <int DIM>
+__device__ __forceinline__ void split_row(int64_t row, const BoxGrid& bg,
+                                          bool modes, int (&idx)[3]) {
+#pragma unroll
+    for (int d = DIM - 2; d >= 0; --d) {
+        const int ext = modes ? bg.N[d] : bg.n[d];
+        idx[d] = (int)(row % ext);
+        row /= ext;
     }
 }
 
@@ -76,20 +82,20 @@ __device__ __forceinline__ bool row_elem(const RowSplit& rs, int64_t* row, int* 
     return *e < rs.per_row;
 }
 
-template <typename G>
+template <int DIM, typename G>
 __global__ void __launch_bounds__(256)
 k_crop(const G* __restrict__ grid, float2* __restrict__ fk, DecPtrs dec,
        BoxGrid bg, RowSplit rs, int64_t nrows) {
-    const int dim = bg.dim;
-    const int L = dim - 1;                    // innermost dim index
+    constexpr int L = DIM - 1;                // innermost dim index
     int64_t row;
     int m_in;
     if (!row_elem(rs, &row, &m_in) || row >= nrows) return;
     const int v = blockIdx.y;
     int m[3] = {0, 0, 0};
-    split_row(row, bg.N, dim, m);
+    split_row<DIM>(row, bg, true, m);
     int64_t rrow = 0;
     float dout = 1.0f;
+#pragma unroll
     for (int d = 0; d < L; ++d) {
         int r = m[d] - bg.N[d] / 2;
         if (r < 0) r += bg.n[d];
@@ -125,22 +131,22 @@ __device__ __forceinline__ void store_pair(double2* p, float4 v) {
     p[1] = make_double2(v.z, v.w);
 }
 
-template <typename H_T>
+template <int DIM, typename H_T>
 __global__ void __launch_bounds__(256)
 k_pad(const float2* __restrict__ f, H_T* __restrict__ H, DecPtrs dec,
       BoxGrid bg, RowSplit rs, int64_t nrows) {
-    const int dim = bg.dim;
-    const int L = dim - 1;
+    constexpr int L = DIM - 1;
     int64_t row;
     int pair;
     if (!row_elem(rs, &row, &pair) || row >= nrows) return;
     const int r0 = 2 * pair;
     const int v = blockIdx.y;
     int r[3] = {0, 0, 0};
-    split_row(row, bg.n, dim, r);
+    split_row<DIM>(row, bg, false, r);
     bool inband = true;
     int64_t mrow = 0;
     float dout = 1.0f;
+#pragma unroll
     for (int d = 0; d < L; ++d) {
         int q = r[d];
         if (q >= bg.n[d] - bg.N[d] / 2) q -= bg.n[d];
@@ -155,17 +161,32 @@ k_pad(const float2* __restrict__ f, H_T* __restrict__ H, DecPtrs dec,
     if (inband) {
         const float2* frow = f + v * bg.K + mrow * bg.N[L];
         const int lo = bg.n[L] - bg.N[L] / 2;     // first negative-mode cell
+        int q0 = r0;
+        if (q0 >= lo) q0 -= bg.n[L];
+        const int m0 = q0 + bg.N[L] / 2;          // mode of cell r0
+        const float* dl = dec.d[L];
+        if (m0 >= 0 && m0 + 1 < bg.N[L] && r0 + 1 != lo &&
+            (reinterpret_cast<uintptr_t>(frow + m0) & 15) == 0 &&
+            (reinterpret_cast<uintptr_t>(dl + m0) & 7) == 0) {
+            // both cells in band with consecutive modes whose addresses
+            // are aligned (the caller's array may be 8-byte aligned only):
+            // one 16-byte strength load, one 8-byte correction load
+            const float4 g = __ldg(reinterpret_cast<const float4*>(frow + m0));
+            float2 dd = __ldg(reinterpret_cast<const float2*>(dl + m0));
+            if (L != 0) { dd.x *= dout; dd.y *= dout; }
+            out = make_float4(g.x * dd.x, g.y * dd.x, g.z * dd.y, g.w * dd.y);
+        } else {
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-            int q = r0 + e;
-            if (q >= lo) q -= bg.n[L];
-            const int mi = q + bg.N[L] / 2;
-            if (mi >= 0 && mi < bg.N[L]) {
-                const float dd = (L == 0) ? __ldg(dec.d[0] + mi)
-                                          : dout * __ldg(dec.d[L] + mi);
-                const float2 g = __ldg(frow + mi);
-                if (e == 0) { out.x = g.x * dd; out.y = g.y * dd; }
-                else        { out.z = g.x * dd; out.w = g.y * dd; }
+            for (int e = 0; e < 2; ++e) {
+                int q = r0 + e;
+                if (q >= lo) q -= bg.n[L];
+                const int mi = q + bg.N[L] / 2;
+                if (mi >= 0 && mi < bg.N[L]) {
+                    const float dd = (L == 0) ? __ldg(dl + mi) : dout * __ldg(dl + mi);
+                    const float2 g = __ldg(frow + mi);
+                    if (e == 0) { out.x = g.x * dd; out.y = g.y * dd; }
+                    else        { out.z = g.x * dd; out.w = g.y * dd; }
+                }
             }
         }
     }
@@ -226,12 +247,16 @@ void launch_crop(int dim, const int64_t* N, const int64_t* n,
     for (int v0 = 0; v0 < nvec; v0 += 65535) {
         const int nv = std::min(65535, nvec - v0);
         dim3 g((unsigned)blocks, (unsigned)nv);
-        if (grid64)
-            k_crop<<<g, 256, 0, st>>>((const double2*)grid + v0 * bg.ncells,
-                                      fk + v0 * bg.K, make_dec(dec), bg, rs, rows);
-        else
-            k_crop<<<g, 256, 0, st>>>((const float2*)grid + v0 * bg.ncells,
-                                      fk + v0 * bg.K, make_dec(dec), bg, rs, rows);
+        NUFFT_DIM_SWITCH(dim, {
+            if (grid64)
+                k_crop<DIM><<<g, 256, 0, st>>>((const double2*)grid + v0 * bg.ncells,
+                                               fk + v0 * bg.K, make_dec(dec), bg, rs,
+                                               rows);
+            else
+                k_crop<DIM><<<g, 256, 0, st>>>((const float2*)grid + v0 * bg.ncells,
+                                               fk + v0 * bg.K, make_dec(dec), bg, rs,
+                                               rows);
+        });
         NUFFT_LAUNCH("k_crop");
     }
 }
@@ -249,12 +274,14 @@ void launch_pad(int dim, const int64_t* N, const int64_t* n,
     for (int v0 = 0; v0 < nvec; v0 += 65535) {
         const int nv = std::min(65535, nvec - v0);
         dim3 g((unsigned)blocks, (unsigned)nv);
-        if (grid64)
-            k_pad<<<g, 256, 0, st>>>(f + v0 * bg.K, (double2*)H + v0 * bg.ncells,
-                                     make_dec(dec), bg, rs, rows);
-        else
-            k_pad<<<g, 256, 0, st>>>(f + v0 * bg.K, (float2*)H + v0 * bg.ncells,
-                                     make_dec(dec), bg, rs, rows);
+        NUFFT_DIM_SWITCH(dim, {
+            if (grid64)
+                k_pad<DIM><<<g, 256, 0, st>>>(f + v0 * bg.K, (double2*)H + v0 * bg.ncells,
+                                              make_dec(dec), bg, rs, rows);
+            else
+                k_pad<DIM><<<g, 256, 0, st>>>(f + v0 * bg.K, (float2*)H + v0 * bg.ncells,
+                                              make_dec(dec), bg, rs, rows);
+        });
         NUFFT_LAUNCH("k_pad");
     }
 }

@@ -354,7 +354,7 @@ k_interp1_stream(const float2* __restrict__ grid, int nvg, int msub,
                  int64_t ostride, TileGeom tg, int* __restrict__ err) {
     extern __shared__ __align__(128) unsigned char sraw[];
     __shared__ __align__(8) uint64_t bar[2];
-    __shared__ int s_next;
+    __shared__ int ring[2];
     __shared__ int s_ok;
     const StreamLayout L = stream_layout(tg.tcells, msub, nvg, phase != nullptr);
     const uint64_t pol = l2_evict_last_policy();
@@ -362,7 +362,6 @@ k_interp1_stream(const float2* __restrict__ grid, int nvg, int msub,
         mbar_init(&bar[0], 1);
         mbar_init(&bar[1], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        s_next = atomicAdd(&sched[0], 1);
         s_ok = (smem_addr(sraw) & 127u) == 0;
     }
     __syncthreads();
@@ -390,30 +389,28 @@ k_interp1_stream(const float2* __restrict__ grid, int nvg, int msub,
             bulk_load(st + L.phase_off, phase + q.c0, (uint32_t)(q.c1 - q.c0) * 8,
                       &bar[b]);
     };
-    int cur = s_next;
+    // ring[b]: subproblem loaded into stage b.  Thread 0 claims two ahead,
+    // so each iteration needs a single CTA barrier (which also releases the
+    // stage it consumed and agrees on a failed wait).
+    if (threadIdx.x == 0) {
+        for (int k = 0; k < 2; ++k) {
+            ring[k] = atomicAdd(&sched[0], 1);
+            if (ring[k] < nsub) issue(stream_sub(subs[ring[k]], tg, L.tile_cells), k);
+        }
+    }
+    __syncthreads();
+    int cur = ring[0];
     int b = 0;
     uint32_t parity0 = 0u, parity1 = 0u;
-    if (cur < nsub && threadIdx.x == 0) issue(stream_sub(subs[cur], tg, L.tile_cells), 0);
-    bool failed = false, pending_other = false;
+    bool failed = false;
     while (cur < nsub) {
-        __syncthreads();                       // stage b ^ 1 and s_next free
-        if (threadIdx.x == 0) s_next = atomicAdd(&sched[0], 1);
-        __syncthreads();
-        const int nxt = s_next;
-        pending_other = nxt < nsub;
-        if (pending_other && threadIdx.x == 0)
-            issue(stream_sub(subs[nxt], tg, L.tile_cells), b ^ 1);
         const StreamSub q = stream_sub(subs[cur], tg, L.tile_cells);
         const bool ok = mbar_wait(&bar[b], b ? parity1 : parity0);
         if (b) parity1 ^= 1u; else parity0 ^= 1u;
-        if (__syncthreads_or(!ok)) {
-            failed = true;
-            break;
-        }
         unsigned char* st = stage(b);
         const float2* tile = reinterpret_cast<const float2*>(st);
         int xoff = q.o - q.g0;
-        if (!q.interior) {
+        if (!q.interior) {                     // uniform across the CTA
             float2* tw = reinterpret_cast<float2*>(st);
             for (int c = threadIdx.x; c < tg.tcells; c += blockDim.x) {
                 const int g = wrap_tile(q.o + c, tg.n[0]);
@@ -429,7 +426,7 @@ k_interp1_stream(const float2* __restrict__ grid, int nvg, int msub,
         const float2* sh = phase ? reinterpret_cast<const float2*>(st + L.phase_off) +
                                        (q.start - q.c0)
                                  : nullptr;
-        for (int t = threadIdx.x; t < q.cnt; t += blockDim.x) {
+        for (int t = threadIdx.x; ok && t < q.cnt; t += blockDim.x) {
             const int2 cl = sc[t];
             const int l0 = cl.x - q.o;
             float wgt[W];
@@ -451,12 +448,22 @@ k_interp1_stream(const float2* __restrict__ grid, int nvg, int msub,
                 st_keep(out + v * ostride + dst, acc, pol);
             }
         }
-        cur = nxt;
+        if (__syncthreads_or(!ok)) {           // stage b consumed by all
+            failed = true;
+            break;
+        }
+        if (threadIdx.x == 0) {                // refill stage b, two ahead
+            const int nn = atomicAdd(&sched[0], 1);
+            ring[b] = nn;
+            if (nn < nsub) issue(stream_sub(subs[nn], tg, L.tile_cells), b);
+        }
+        cur = ring[b ^ 1];
         b ^= 1;
     }
     if (failed && threadIdx.x == 0) {
         atomicOr(err, kErrTileWait);
-        if (pending_other) mbar_wait(&bar[b ^ 1], b ? parity0 : parity1);
+        // the other stage may hold a copy in flight: wait for it (bounded)
+        if (ring[b ^ 1] < nsub) mbar_wait(&bar[b ^ 1], b ? parity0 : parity1);
     }
     scheduler_done(sched);
 }
