@@ -142,7 +142,7 @@ k_interp_tma(const __grid_constant__ CUtensorMap tmap, const float2* __restrict_
              int* __restrict__ err) {
     extern __shared__ __align__(128) float2 sbuf[];     // [2][nvg][T0][T1][B2]
     __shared__ __align__(8) uint64_t bar[2];
-    __shared__ int s_next;
+    __shared__ int ring[2];
     __shared__ int s_tma;                                // 0: all tiles by hand
     constexpr int U = 2;
     const int S = B2, PS = tg.T[1] * B2;
@@ -155,7 +155,6 @@ k_interp_tma(const __grid_constant__ CUtensorMap tmap, const float2* __restrict_
         mbar_init(&bar[0], 1);
         mbar_init(&bar[1], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        s_next = atomicAdd(&sched[0], 1);
         s_tma = (smem_addr(sbuf) & 127u) == 0;
     }
     __syncthreads();
@@ -169,41 +168,36 @@ k_interp_tma(const __grid_constant__ CUtensorMap tmap, const float2* __restrict_
             tma_load_4d(sbuf + ((size_t)b * nvg + v) * TS, &tmap, bn.x0, bn.o[1],
                         bn.o[0], v0 + v, &bar[b]);
     };
-    int cur = s_next;
-    int b = 0;
-    uint32_t parity[2] = {0u, 0u};
-    bool pending[2] = {false, false};
-    if (cur < nsub && threadIdx.x == 0) {
-        const TmaBin bn = tma_bin(subs[cur].z, tg, B2, use_tma);
-        if (bn.interior) issue(bn, 0);
+    // ring[b]: subproblem whose tile occupies buffer b.  Thread 0 claims two
+    // ahead, so each subproblem needs one CTA barrier (which also releases
+    // the buffer it consumed and agrees on a failed wait).
+    if (threadIdx.x == 0) {
+        for (int k = 0; k < 2; ++k) {
+            ring[k] = atomicAdd(&sched[0], 1);
+            if (ring[k] < nsub) {
+                const TmaBin nb = tma_bin(subs[ring[k]].z, tg, B2, use_tma);
+                if (nb.interior) issue(nb, k);
+            }
+        }
     }
-    if (cur < nsub) pending[0] = tma_bin(subs[cur].z, tg, B2, use_tma).interior;
+    __syncthreads();
+    int cur = ring[0];
+    int b = 0;
+    uint32_t parity0 = 0u, parity1 = 0u;
     bool failed = false;
     while (cur < nsub) {
-        __syncthreads();                        // previous s_next consumed
-        if (threadIdx.x == 0) s_next = atomicAdd(&sched[0], 1);
-        __syncthreads();
-        const int nxt = s_next;
-        if (nxt < nsub) {
-            const TmaBin nb = tma_bin(subs[nxt].z, tg, B2, use_tma);
-            pending[b ^ 1] = nb.interior;
-            if (nb.interior && threadIdx.x == 0) issue(nb, b ^ 1);
-        }
         const int4 sb = subs[cur];
         const TmaBin bn = tma_bin(sb.z, tg, B2, use_tma);
         float2* tile = sbuf + (size_t)b * nvg * TS;
+        bool ok = true;
         int xoff;
         if (bn.interior) {
-            const bool ok = mbar_wait(&bar[b], parity[b]);
-            parity[b] ^= 1u;
-            pending[b] = false;
-            if (__syncthreads_or(!ok)) {
-                failed = true;
-                break;
-            }
+            ok = mbar_wait(&bar[b], b ? parity1 : parity0);
+            if (b) parity1 ^= 1u; else parity0 ^= 1u;
             xoff = bn.o[2] - bn.x0;
         } else {
-            // wrapped tile: per-thread loads into the same padded layout
+            // wrapped tile (uniform across the CTA): per-thread loads into
+            // the same padded layout
             for (int q = threadIdx.x; q < tg.tcells; q += blockDim.x) {
                 const int64_t g = tile_to_global<3>(q, bn.o, tg);
                 const int row = (int)__umulhi((unsigned)q, tg.tdiv[2]);
@@ -215,7 +209,7 @@ k_interp_tma(const __grid_constant__ CUtensorMap tmap, const float2* __restrict_
             xoff = 0;
         }
         const int start = sb.x, cnt = sb.y;
-        for (int base = 0; base < cnt; base += U * blockDim.x) {
+        for (int base = 0; ok && base < cnt; base += U * blockDim.x) {
             int2 cl[U][3];
             int64_t dst[U];
             float2 ph[U];
@@ -233,18 +227,18 @@ k_interp_tma(const __grid_constant__ CUtensorMap tmap, const float2* __restrict_
                 if (base + u * (int)blockDim.x + (int)threadIdx.x >= cnt) break;
                 float wgt[3][W];
                 int l0[3];
-                bool ok = true;
+                bool inb = true;
 #pragma unroll
                 for (int d = 0; d < 3; ++d) {
                     l0[d] = cl[u][d].x - bn.o[d];
-                    ok &= (unsigned)l0[d] < (unsigned)tg.m[d];
+                    inb &= (unsigned)l0[d] < (unsigned)tg.m[d];
                     kernel_weights<W>(__int_as_float(cl[u][d].y), tg, wgt[d]);
                 }
                 const int tb = l0[0] * PS + l0[1] * S + l0[2] + xoff;
                 for (int v = 0; v < nvg; ++v) {
                     // gather3 rotates the x-weights W times: back in order
                     float2 acc = make_float2(0.0f, 0.0f);
-                    if (ok) {
+                    if (inb) {
                         acc = gather3<W>(tile + v * TS, S, PS, tb, wgt);
                         if (phase) acc = cmul(acc, ph[u]);
                     }
@@ -255,15 +249,28 @@ k_interp_tma(const __grid_constant__ CUtensorMap tmap, const float2* __restrict_
                 }
             }
         }
-        cur = nxt;
+        if (__syncthreads_or(!ok)) {           // buffer b consumed by all
+            failed = true;
+            break;
+        }
+        if (threadIdx.x == 0) {                // refill buffer b, two ahead
+            const int nn = atomicAdd(&sched[0], 1);
+            ring[b] = nn;
+            if (nn < nsub) {
+                const TmaBin nb = tma_bin(subs[nn].z, tg, B2, use_tma);
+                if (nb.interior) issue(nb, b);
+            }
+        }
+        cur = ring[b ^ 1];
         b ^= 1;
     }
     if (failed && threadIdx.x == 0) {
         atomicOr(err, kErrTileWait);
         // the other buffer may still have a copy in flight: wait for it
         // (bounded) before the CTA's shared memory is released
-        const int o = b ^ 1;
-        if (pending[o]) mbar_wait(&bar[o], parity[o]);
+        const int o = ring[b ^ 1];
+        if (o < nsub && tma_bin(subs[o].z, tg, B2, use_tma).interior)
+            mbar_wait(&bar[b ^ 1], b ? parity0 : parity1);
     }
     scheduler_done(sched);
 }
