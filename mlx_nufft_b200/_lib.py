@@ -70,6 +70,7 @@ class NufftPlanInfo(ctypes.Structure):
         ("kernel_launches", ctypes.c_int64),
         ("fft_execs", ctypes.c_int64),
         ("fft64", ctypes.c_int),
+        ("fft_own", ctypes.c_int),
     ]
 
 

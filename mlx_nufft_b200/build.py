@@ -27,7 +27,7 @@ LIB = os.path.join(HERE, "libnufft_b200.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 SOURCES = ["sizing.cpp", "points.cu", "spread.cu", "interp.cu", "interp_tma.cu",
-           "deconv.cu", "plan.cu", "noalloc.cu"]
+           "deconv.cu", "fft1.cu", "plan.cu", "noalloc.cu"]
 
 
 def _cuda_home():

@@ -1,0 +1,473 @@
+// fft1.cu -- two-pass FFT of power-of-two 1-D fine grids, fused with the
+// type-2 / type-3 pad and the type-1 crop.
+//
+// The reference's 1-D execute is pad (or crop) + one FFT of the n_up-cell
+// fine grid (mlx_nufft/nd.py:878-906 and 416-435 around the FFT call).  For
+// n = N1 x N2 (powers of two, 2^12 <= n <= 2^22) the FFT here is the
+// four-step decomposition
+//
+//   X[k1 + N1 k2] = sum_{n2} W_N2^{n2 k2} W_n^{n2 k1} sum_{n1} W_N1^{n1 k1} x[n1 N2 + n2]
+//
+// in two kernels, each a batch of shared-memory FFTs over C adjacent
+// columns (C = 8 up to length 1024, else 4: every global access moves
+// 32- or 64-byte segments):
+//   pass 1: columns n2 of length N1.  Its loads ARE the pad: cell r of the
+//           fine grid is mode m = (r >= n - N/2 ? r - n : r) + N/2 times the
+//           correction dec[m] when 0 <= m < N, else zero (no zero is read
+//           or written); the inter-pass twiddle W_n^{k1 n2} is applied on
+//           the store to a scratch grid A[k1][n2].
+//   pass 2: rows k1 of A (length N2), stored in natural order X (type 2 /
+//           type 3), or -- type 1 -- only the in-band cells, times dec, in
+//           mode order (the crop).
+// cuFFT's own transform of such a grid is also two passes, plus a separate
+// pad kernel that writes (and the FFT then reads) the whole zero-padded grid.
+//
+// Inside a CTA a length-L FFT is a Stockham sequence of radix-32/16/8
+// stages (log2 L split as evenly as possible over ceil(log2 L / 5) stages:
+// 1024 = 32 x 32, 2048 = 16 x 16 x 8).  The first stage loads its inputs
+// from global memory straight into registers and the last stores its
+// outputs straight to global memory; between stages each thread's R-point
+// DFTs run in registers and exchange through shared memory, whose
+// addresses a are padded to a + a/16 so that the strided stage stores stay
+// free of bank conflicts.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+#include <set>
+#include <type_traits>
+#include <vector>
+
+#include "internal.h"
+
+namespace nufft {
+namespace {
+
+constexpr int kFftThreads = 256;
+
+// Columns per CTA at length 2048, and resident CTAs per SM the kernels are
+// compiled for (caps their registers at 128; measured on 2^21 cells: pass 1
+// 18.4 us vs 21.1 uncapped, 2 rows per CTA at length 2048 slower).
+#ifndef NUFFT_FFT_COLS_2048
+#define NUFFT_FFT_COLS_2048 4
+#endif
+#ifndef NUFFT_FFT_MINB_COLS
+#define NUFFT_FFT_MINB_COLS 2
+#endif
+#ifndef NUFFT_FFT_MINB_ROWS
+#define NUFFT_FFT_MINB_ROWS 2
+#endif
+
+__host__ __device__ constexpr int ilog2(int x) {
+    int k = 0;
+    while ((1 << k) < x) ++k;
+    return k;
+}
+
+// Columns (pass 1) / rows (pass 2) per CTA.
+__host__ __device__ constexpr int fft_cols(int L) {
+    return L <= 1024 ? 8 : NUFFT_FFT_COLS_2048;
+}
+
+// Radix of the stage that starts at span NS (see the file comment).
+__host__ __device__ constexpr int stage_radix(int L, int NS) {
+    const int k = ilog2(L), st = (k + 4) / 5;
+    const int done = ilog2(NS);
+    int t = 0, acc = 0;
+    while (acc < done) {
+        acc += k / st + (t < k % st ? 1 : 0);
+        ++t;
+    }
+    return 1 << (k / st + (t < k % st ? 1 : 0));
+}
+
+__device__ __forceinline__ int fpad(int a) { return a + (a >> 4); }
+
+__host__ __device__ constexpr int fft_data_cells(int L) {
+    return (L * fft_cols(L)) + ((L * fft_cols(L)) >> 4);
+}
+
+__device__ __forceinline__ float2 cmulf(float2 a, float2 b) {
+    return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
+}
+
+// x * W_32^m, W_32 = exp(-2 pi i / 32) (INV: its conjugate); m in 0..15,
+// a compile-time constant once the register DFT is unrolled.
+template <bool INV>
+__device__ __forceinline__ float2 rot32(float2 x, int m) {
+    constexpr float a1 = 0.98078528040323044f;   // cos(pi / 16)
+    constexpr float b1 = 0.19509032201612827f;   // sin(pi / 16)
+    constexpr float a2 = 0.92387953251128674f;   // cos(pi / 8)
+    constexpr float b2 = 0.38268343236508977f;   // sin(pi / 8)
+    constexpr float a3 = 0.83146961230254524f;   // cos(3 pi / 16)
+    constexpr float b3 = 0.55557023301960218f;   // sin(3 pi / 16)
+    constexpr float h = 0.70710678118654752f;    // cos(pi / 4)
+    float c, s;                                  // W_32^m = c - i s
+    switch (m) {
+        case 0: return x;
+        case 8: return INV ? make_float2(-x.y, x.x) : make_float2(x.y, -x.x);
+        case 1: c = a1; s = b1; break;
+        case 2: c = a2; s = b2; break;
+        case 3: c = a3; s = b3; break;
+        case 4: c = h; s = h; break;
+        case 5: c = b3; s = a3; break;
+        case 6: c = b2; s = a2; break;
+        case 7: c = b1; s = a1; break;
+        case 9: c = -b1; s = a1; break;
+        case 10: c = -b2; s = a2; break;
+        case 11: c = -b3; s = a3; break;
+        case 12: c = -h; s = h; break;
+        case 13: c = -a3; s = b3; break;
+        case 14: c = -a2; s = b2; break;
+        default: c = -a1; s = b1; break;         // 15
+    }
+    return INV ? make_float2(x.x * c - x.y * s, x.y * c + x.x * s)
+               : make_float2(x.x * c + x.y * s, x.y * c - x.x * s);
+}
+
+template <int R>
+__host__ __device__ constexpr int bit_reverse(int i) {
+    int r = 0;
+    for (int b = 1; b < R; b <<= 1) {
+        r = (r << 1) | (i & 1);
+        i >>= 1;
+    }
+    return r;
+}
+
+// In-register R-point DFT (R = 2 .. 32), radix-2 decimation in time.
+template <int R, bool INV>
+__device__ __forceinline__ void dft_reg(float2 (&v)[R]) {
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        const int j = bit_reverse<R>(i);
+        if (j > i) {
+            const float2 t = v[i];
+            v[i] = v[j];
+            v[j] = t;
+        }
+    }
+#pragma unroll
+    for (int h = 1; h < R; h <<= 1) {
+#pragma unroll
+        for (int s = 0; s < R; s += 2 * h) {
+#pragma unroll
+            for (int k = 0; k < h; ++k) {
+                const float2 a = v[s + k];
+                const float2 b = rot32<INV>(v[s + k + h], k * (16 / h));  // W_2h^k
+                v[s + k] = make_float2(a.x + b.x, a.y + b.y);
+                v[s + k + h] = make_float2(a.x - b.x, a.y - b.y);
+            }
+        }
+    }
+}
+
+// Stockham stages NS, NS*R, ... of a length-L FFT over the CTA's C =
+// fft_cols(L) columns.  The first stage takes its inputs from load(c, i)
+// (row i of column c); the last hands each butterfly's outputs to
+// store(c, base, stride, v): v[r] is row base + r * stride of column c.
+// In between, element (i, c) lives at s[fpad(i * C + c)].  twL[m] = W_L^m
+// (global, read through L1).
+template <int L, int NS, bool INV, class Load, class Store>
+__device__ __forceinline__ void fft_stages(float2* s, const float2* __restrict__ twL,
+                                           const Load& load, const Store& store) {
+    if constexpr (NS < L) {
+        constexpr int C = fft_cols(L);
+        constexpr int R = stage_radix(L, NS);
+        constexpr bool LAST = NS * R == L;
+        constexpr int NB = (L / R) * C;                 // butterflies
+        constexpr int PER = (NB + kFftThreads - 1) / kFftThreads;
+        float2 v[PER][R];
+#pragma unroll
+        for (int t = 0; t < PER; ++t) {
+            const int bid = threadIdx.x + t * kFftThreads;
+            if (NB % kFftThreads == 0 || bid < NB) {
+                const int c = bid % C, j = bid / C;
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+                    v[t][r] = NS == 1 ? load(c, j + r * (L / R))
+                                      : s[fpad((j + r * (L / R)) * C + c)];
+                if (NS > 1) {
+                    const int k = j % NS;
+#pragma unroll
+                    for (int r = 1; r < R; ++r) {
+                        float2 w = __ldg(twL + r * k * (L / (NS * R)));
+                        if (INV) w.y = -w.y;
+                        v[t][r] = cmulf(v[t][r], w);
+                    }
+                }
+                dft_reg<R, INV>(v[t]);
+            }
+        }
+        if constexpr (LAST) {
+#pragma unroll
+            for (int t = 0; t < PER; ++t) {
+                const int bid = threadIdx.x + t * kFftThreads;
+                if (NB % kFftThreads == 0 || bid < NB) {
+                    const int c = bid % C, j = bid / C;
+                    store(c, (j / NS) * NS * R + (j % NS), NS, v[t]);
+                }
+            }
+        } else {
+            if (NS > 1) __syncthreads();               // all reads of s done
+#pragma unroll
+            for (int t = 0; t < PER; ++t) {
+                const int bid = threadIdx.x + t * kFftThreads;
+                if (NB % kFftThreads == 0 || bid < NB) {
+                    const int c = bid % C, j = bid / C;
+                    const int base = (j / NS) * NS * R + (j % NS);
+#pragma unroll
+                    for (int r = 0; r < R; ++r)
+                        s[fpad((base + r * NS) * C + c)] = v[t][r];
+                }
+            }
+            __syncthreads();
+            fft_stages<L, NS * R, INV>(s, twL, load, store);
+        }
+    }
+}
+
+// Inter-pass twiddles are taken exactly from the tables every kTwExact
+// rows and by complex multiplication by the row step in between (at most
+// kTwExact - 1 products, a few fp32 ulps).
+constexpr int kTwExact = 4;
+
+// Pass 1: columns c0 .. c0 + C - 1 of the fine grid (length L = N1), read
+// either as padded modes (PAD: in = modes of box N with correction dec)
+// or as a plain grid; A[k1 * N2 + n2] = W_n^{k1 n2} * column FFT.
+// twL = W_N1 table, twn[e] = W_n^e for e < N2; N2 = 1 << lg2.
+template <int L, bool INV, bool PAD>
+__global__ void __launch_bounds__(kFftThreads, NUFFT_FFT_MINB_COLS)
+k_fft1_cols(const float2* __restrict__ in, int64_t in_stride, int64_t N,
+            const float* __restrict__ dec, int n, int lg2,
+            const float2* __restrict__ twL, const float2* __restrict__ twn,
+            float2* __restrict__ A) {
+    constexpr int C = fft_cols(L);
+    extern __shared__ float2 s[];
+    const int v = blockIdx.y;
+    const int c0 = blockIdx.x * C;
+    in += v * in_stride;
+    A += (int64_t)v * n;
+    const int64_t lo = n - N / 2;                 // first negative-mode cell
+    const int64_t half = N / 2;
+    const uint32_t emask = (uint32_t)(n - 1), lmask = (1u << lg2) - 1u;
+    auto load = [&](int c, int i) {
+        const int64_t cell = ((int64_t)i << lg2) + c0 + c;
+        float2 x = make_float2(0.0f, 0.0f);
+        if (PAD) {
+            const int64_t m = (cell >= lo ? cell - n : cell) + half;
+            if (m >= 0 && m < N) {
+                const float d = __ldg(dec + m);
+                const float2 g = __ldg(in + m);
+                x = make_float2(g.x * d, g.y * d);
+            }
+        } else {
+            x = __ldg(in + cell);
+        }
+        return x;
+    };
+    // W_n^e from the tables: e = eh * N2 + el, W_n^{eh N2} = W_L^{eh}
+    auto wn = [&](uint32_t e) {
+        e &= emask;
+        float2 w = cmulf(__ldg(twL + (e >> lg2)), __ldg(twn + (e & lmask)));
+        if (INV) w.y = -w.y;
+        return w;
+    };
+    auto store = [&](int c, int base, int stride, auto& vals) {
+        constexpr int R = std::extent<std::remove_reference_t<decltype(vals)>>::value;
+        const uint32_t n2 = (uint32_t)(c0 + c);
+        const float2 step = wn((uint32_t)stride * n2);
+        float2 w = make_float2(1.0f, 0.0f);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int k1 = base + r * stride;
+            w = (r % kTwExact == 0) ? wn((uint32_t)k1 * n2) : cmulf(w, step);
+            A[((int64_t)k1 << lg2) + n2] = cmulf(vals[r], w);
+        }
+    };
+    fft_stages<L, 1, INV>(s, twL, load, store);
+}
+
+// Pass 2: rows r0 .. r0 + C - 1 of A (length L = N2).  CROP: fk[m] =
+// X[k] * dec[m] for the in-band cells k (mode m as in pass 1), else X[k]
+// (natural order).
+template <int L, bool INV, bool CROP>
+__global__ void __launch_bounds__(kFftThreads, NUFFT_FFT_MINB_ROWS)
+k_fft1_rows(const float2* __restrict__ A, int N1, int n,
+            const float2* __restrict__ twL, float2* __restrict__ out,
+            int64_t out_stride, int64_t N, const float* __restrict__ dec) {
+    constexpr int C = fft_cols(L);
+    extern __shared__ float2 s[];
+    const int v = blockIdx.y;
+    const int r0 = blockIdx.x * C;
+    A += (int64_t)v * n;
+    out += v * out_stride;
+    const int64_t lo = n - N / 2;
+    const int64_t half = N / 2;
+    auto load = [&](int c, int j) {
+        return __ldg(A + (int64_t)(r0 + c) * L + j);
+    };
+    auto store = [&](int c, int base, int stride, auto& vals) {
+        constexpr int R = std::extent<std::remove_reference_t<decltype(vals)>>::value;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int64_t k = (int64_t)(r0 + c) + (int64_t)N1 * (base + r * stride);
+            const float2 x = vals[r];
+            if (CROP) {
+                const int64_t m = (k >= lo ? k - n : k) + half;
+                if (m >= 0 && m < N) {
+                    const float d = __ldg(dec + m);
+                    out[m] = make_float2(x.x * d, x.y * d);
+                }
+            } else {
+                out[k] = x;
+            }
+        }
+    };
+    fft_stages<L, 1, INV>(s, twL, load, store);
+}
+
+template <int L>
+size_t fft_smem() {
+    return sizeof(float2) * (size_t)fft_data_cells(L);
+}
+
+// Compile-time dispatch over the supported lengths 64..2048.
+#define NUFFT_FFT_LEN_SWITCH(len, ...)                                 \
+    switch (len) {                                                     \
+        case 64: { constexpr int L = 64; __VA_ARGS__; } break;         \
+        case 128: { constexpr int L = 128; __VA_ARGS__; } break;       \
+        case 256: { constexpr int L = 256; __VA_ARGS__; } break;       \
+        case 512: { constexpr int L = 512; __VA_ARGS__; } break;       \
+        case 1024: { constexpr int L = 1024; __VA_ARGS__; } break;     \
+        case 2048: { constexpr int L = 2048; __VA_ARGS__; } break;     \
+        default: fail(-1, "fft1: unsupported length");                  \
+    }
+
+// Dynamic shared memory opt-in, and the largest shared-memory carveout so
+// that as many CTAs as the registers allow stay resident (once per kernel).
+void prepare(const void* kernel, size_t smem) {
+    ensure_smem(kernel, smem);
+    static std::mutex mu;
+    static std::set<const void*> done;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.insert(kernel).second)
+        NUFFT_CUDA(cudaFuncSetAttribute(
+            kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+            (int)cudaSharedmemCarveoutMaxShared));
+}
+
+// pass 1 for nv vectors
+void run_cols(const Fft1& f, const float2* in, int64_t in_stride, int64_t N,
+              const float* dec, bool pad, bool inv, float2* A, int nv,
+              cudaStream_t st) {
+    NUFFT_FFT_LEN_SWITCH(f.N1, {
+        const size_t smem = fft_smem<L>();
+        dim3 g((unsigned)(f.N2 / fft_cols(L)), (unsigned)nv);
+        auto launch = [&](auto k) {
+            prepare((const void*)k, smem);
+            k<<<g, kFftThreads, smem, st>>>(in, in_stride, N, dec, f.n, ilog2(f.N2),
+                                            f.tw, f.tw + f.N1 + f.N2, A);
+        };
+        if (pad)
+            inv ? launch(k_fft1_cols<L, true, true>) : launch(k_fft1_cols<L, false, true>);
+        else
+            inv ? launch(k_fft1_cols<L, true, false>) : launch(k_fft1_cols<L, false, false>);
+    });
+    NUFFT_LAUNCH("k_fft1_cols");
+}
+
+// pass 2 for nv vectors
+void run_rows(const Fft1& f, const float2* A, bool crop, bool inv, float2* out,
+              int64_t out_stride, int64_t N, const float* dec, int nv,
+              cudaStream_t st) {
+    NUFFT_FFT_LEN_SWITCH(f.N2, {
+        const size_t smem = fft_smem<L>();
+        dim3 g((unsigned)(f.N1 / fft_cols(L)), (unsigned)nv);
+        auto launch = [&](auto k) {
+            prepare((const void*)k, smem);
+            k<<<g, kFftThreads, smem, st>>>(A, f.N1, f.n, f.tw + f.N1, out, out_stride,
+                                            N, dec);
+        };
+        if (crop)
+            inv ? launch(k_fft1_rows<L, true, true>) : launch(k_fft1_rows<L, false, true>);
+        else
+            inv ? launch(k_fft1_rows<L, true, false>) : launch(k_fft1_rows<L, false, false>);
+    });
+    NUFFT_LAUNCH("k_fft1_rows");
+}
+
+}  // namespace
+
+bool fft1_supported(int64_t n) {
+    return n >= (1 << 12) && n <= (1 << 22) && (n & (n - 1)) == 0;
+}
+
+void fft1_init(Fft1* f, int64_t n) {
+    fft1_free(f);
+    if (!fft1_supported(n)) fail(-1, "fft1: unsupported size");
+    const int k = ilog2((int)n);
+    f->n = (int)n;
+    f->N1 = 1 << (k / 2);
+    f->N2 = 1 << (k - k / 2);
+    // [W_N1^m, m < N1][W_N2^m, m < N2][W_n^m, m < N2], forward sign, from
+    // fp64 host cos/sin rounded once to fp32
+    const double two_pi = 6.283185307179586476925286766559;
+    std::vector<float2> h((size_t)f->N1 + 2 * (size_t)f->N2);
+    auto fill = [&](float2* dst, int count, double len) {
+        for (int m = 0; m < count; ++m) {
+            const double a = two_pi * (double)m / len;
+            dst[m] = make_float2((float)std::cos(a), (float)-std::sin(a));
+        }
+    };
+    fill(h.data(), f->N1, f->N1);
+    fill(h.data() + f->N1, f->N2, f->N2);
+    fill(h.data() + f->N1 + f->N2, f->N2, (double)n);
+    NUFFT_CUDA(cudaMalloc(&f->tw, sizeof(float2) * h.size()));
+    NUFFT_CUDA(cudaMemcpy(f->tw, h.data(), sizeof(float2) * h.size(),
+                          cudaMemcpyHostToDevice));
+}
+
+void fft1_free(Fft1* f) {
+    if (f->tw) cudaFree(f->tw);
+    if (f->tmp) cudaFree(f->tmp);
+    *f = Fft1{};
+}
+
+void fft1_reserve(Fft1* f, int nv) {
+    if (nv <= f->tmp_batch) return;
+    if (f->tmp) {
+        NUFFT_CUDA(cudaDeviceSynchronize());     // scratch may still be in use
+        cudaFree(f->tmp);
+        f->tmp = nullptr;
+        f->tmp_batch = 0;
+    }
+    NUFFT_CUDA(cudaMalloc(&f->tmp, sizeof(float2) * (size_t)f->n * nv));
+    f->tmp_batch = nv;
+}
+
+void fft1_cols(Fft1* f, const float2* in, int64_t N, const float* dec, int nv,
+               bool inv, cudaStream_t st) {
+    fft1_reserve(f, nv);
+    const bool pad = dec != nullptr;
+    const int64_t stride = pad ? N : f->n;
+    for (int v0 = 0; v0 < nv; v0 += 65535) {
+        const int k = std::min(65535, nv - v0);
+        run_cols(*f, in + v0 * stride, stride, N, dec, pad, inv,
+                 f->tmp + (int64_t)v0 * f->n, k, st);
+    }
+}
+
+void fft1_rows(Fft1* f, float2* out, int64_t N, const float* dec, int nv, bool inv,
+               cudaStream_t st) {
+    const bool crop = dec != nullptr;
+    const int64_t stride = crop ? N : f->n;
+    for (int v0 = 0; v0 < nv; v0 += 65535) {
+        const int k = std::min(65535, nv - v0);
+        run_rows(*f, f->tmp + (int64_t)v0 * f->n, crop, inv, out + v0 * stride, stride,
+                 N, dec, k, st);
+    }
+}
+
+}  // namespace nufft

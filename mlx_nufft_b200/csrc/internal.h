@@ -149,6 +149,30 @@ struct PointSet {
     uint32_t* perm_alt = nullptr;
 };
 
+// Raise a kernel's dynamic shared-memory limit to `bytes` when it exceeds
+// the 48 KB default (host-side attribute call, cached per kernel).
+void ensure_smem(const void* kernel, size_t bytes);
+
+// Two-pass FFT of a power-of-two 1-D fine grid (fft1.cu), n = N1 * N2.
+struct Fft1 {
+    int n = 0, N1 = 0, N2 = 0;   // n == 0: not in use
+    float2* tw = nullptr;        // twiddle tables (device)
+    float2* tmp = nullptr;       // pass-1 output, tmp_batch grids
+    int tmp_batch = 0;
+};
+bool fft1_supported(int64_t n);
+void fft1_init(Fft1* f, int64_t n);
+void fft1_free(Fft1* f);
+void fft1_reserve(Fft1* f, int nv);
+// pass 1 into f->tmp: with dec, `in` is nv mode vectors of length N that are
+// padded (times dec) into the fine grid on the fly; without, nv fine grids
+void fft1_cols(Fft1* f, const float2* in, int64_t N, const float* dec, int nv,
+               bool inv, cudaStream_t st);
+// pass 2 from f->tmp: with dec, the in-band cells times dec into nv mode
+// vectors of length N (crop); without, nv fine grids in natural order
+void fft1_rows(Fft1* f, float2* out, int64_t N, const float* dec, int nv, bool inv,
+               cudaStream_t st);
+
 // CTAs for a persistent launch of `kernel` (256 threads, `smem` bytes):
 // resident CTAs per SM x SMs, capped at `work` items.
 int persistent_grid(const void* kernel, size_t smem, int64_t work,

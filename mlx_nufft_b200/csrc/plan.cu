@@ -144,6 +144,7 @@ struct nufft_plan_s {
     float2* gspread = nullptr;
     float2* gfft = nullptr;
     std::map<int, cufftHandle> ffts;
+    Fft1 fft1;                 // two-pass 1-D FFT (fft1.cu), when in use
     bool profile = false;
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     bool ev_recorded = false;
@@ -707,8 +708,25 @@ const float2* interp_grid32(const nufft_plan_s* p) {
     return (p->fft64 || !on) ? nullptr : p->gfft;
 }
 
+// The two-pass FFT of fft1.cu, with the pad / crop fused into its passes,
+// replaces pad + cuFFT (+ crop) for complex64 1-D grids of power-of-two
+// size (NUFFT_FFT1=0 keeps cuFFT, for tuning).  Set up on first use, since
+// a type-3 plan learns its grid size at setpts.
+bool fft1_wanted(const nufft_plan_s* p) {
+    static const int on = env_int("NUFFT_FFT1", 1);
+    return on && p->dim == 1 && !p->fft64 && fft1_supported(p->nup[0]);
+}
+
+bool use_fft1(nufft_plan_s* p) {
+    if (!fft1_wanted(p)) return false;
+    if (p->fft1.n != p->nup[0]) fft1_init(&p->fft1, p->nup[0]);
+    return true;
+}
+
 void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
                    int stage, cudaStream_t st) {
+    const bool f1 = use_fft1(p);
+    const bool inv = p->isign > 0;
     if (p->type == 1) {
         float2* sg = t1_spread_grid(p);
         if (stage == NUFFT_STAGE_ALL || stage == NUFFT_STAGE_SPREAD) {
@@ -723,21 +741,34 @@ void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
                 record(p, 0, st);
                 record(p, 1, st);
             }
-            if (p->fft64) {
-                launch_widen(sg, (double2*)p->gfft, p->nupcells * nv, st);
-                }
-            run_fft(p, nv, st);
-            record(p, 2, st);
-            launch_crop(p->dim, p->N, p->nup, p->dec, p->gfft, p->fft64, out, nv,
-                        st);
-            record(p, 3, st);
+            if (f1) {                  // pass 1, then pass 2 with the crop
+                fft1_cols(&p->fft1, sg, 0, nullptr, nv, inv, st);
+                record(p, 2, st);
+                fft1_rows(&p->fft1, out, p->N[0], p->dec[0], nv, inv, st);
+                record(p, 3, st);
+            } else {
+                if (p->fft64)
+                    launch_widen(sg, (double2*)p->gfft, p->nupcells * nv, st);
+                run_fft(p, nv, st);
+                record(p, 2, st);
+                launch_crop(p->dim, p->N, p->nup, p->dec, p->gfft, p->fft64, out, nv,
+                            st);
+                record(p, 3, st);
+            }
         }
     } else if (p->type == 2) {
         if (stage == NUFFT_STAGE_ALL || stage == NUFFT_STAGE_SPREAD) {
             record(p, 0, st);
-            launch_pad(p->dim, p->N, p->nup, p->dec, in, p->gfft, p->fft64, nv, st);
-            record(p, 1, st);
-            run_fft(p, nv, st);
+            if (f1) {                  // pass 1 with the pad, then pass 2
+                fft1_cols(&p->fft1, in, p->N[0], p->dec[0], nv, inv, st);
+                record(p, 1, st);
+                fft1_rows(&p->fft1, p->gfft, 0, nullptr, nv, inv, st);
+            } else {
+                launch_pad(p->dim, p->N, p->nup, p->dec, in, p->gfft, p->fft64, nv,
+                           st);
+                record(p, 1, st);
+                run_fft(p, nv, st);
+            }
             record(p, 2, st);
         }
         if (stage == NUFFT_STAGE_SPREAD) {
@@ -760,10 +791,16 @@ void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
         NUFFT_CUDA(cudaMemsetAsync(p->gspread, 0, sizeof(float2) * p->nfcells * nv, st));
         launch_spread(p->src, p->tg_src, p->w, in, p->src.M, nv, p->gspread,
                       p->nvg_src, st);
-        launch_pad(p->dim, p->nf, p->nup, p->dec, p->gspread, p->gfft, p->fft64,
-                   nv, st);
-        record(p, 1, st);
-        run_fft(p, nv, st);
+        if (f1) {
+            fft1_cols(&p->fft1, p->gspread, p->nf[0], p->dec[0], nv, inv, st);
+            record(p, 1, st);
+            fft1_rows(&p->fft1, p->gfft, 0, nullptr, nv, inv, st);
+        } else {
+            launch_pad(p->dim, p->nf, p->nup, p->dec, p->gspread, p->gfft, p->fft64,
+                       nv, st);
+            record(p, 1, st);
+            run_fft(p, nv, st);
+        }
         record(p, 2, st);
         if (!launch_interp_tma(p->tgt, p->tg_tgt, p->w2, interp_tmap(p, p->tg_tgt),
                                interp_grid32(p), nv, out, p->Ntgt, p->d_err, st))
@@ -784,6 +821,7 @@ void ensure_batch(nufft_plan_s* p, int nvec) {
     size_t per = fft_cell_bytes(p) * (size_t)p->nupcells;
     if (p->type == 3) per += sizeof(float2) * (size_t)p->nfcells;
     else if (p->type == 1 && p->fft64) per += sizeof(float2) * (size_t)p->nupcells;
+    if (fft1_wanted(p)) per += sizeof(float2) * (size_t)p->nupcells;  // FFT scratch
     const size_t have = per * (size_t)p->nbatch;
     const int64_t cap = (int64_t)((free_b / 2 + have) / per);
     const int nb = (int)std::min<int64_t>(nvec, std::max<int64_t>(cap, p->nbatch));
@@ -1018,6 +1056,12 @@ int nufft_execute_disjoint(nufft_plan_t p, const void* c, const int32_t* groups,
                 // labels relative to this window; out-of-window -> -1
                 window_labels(groups, p->src.M, g0, ng, shifted, st);
                 launch_spread_groups(p->src, p->tg_src, p->w, fc, shifted, sg, st);
+                if (use_fft1(p)) {
+                    fft1_cols(&p->fft1, sg, 0, nullptr, ng, p->isign > 0, st);
+                    fft1_rows(&p->fft1, fo + (int64_t)g0 * p->K, p->N[0], p->dec[0], ng,
+                              p->isign > 0, st);
+                    continue;
+                }
                 if (p->fft64) launch_widen(sg, (double2*)p->gfft, p->nupcells * ng, st);
                 run_fft(p, ng, st);
                 launch_crop(p->dim, p->N, p->nup, p->dec, p->gfft, p->fft64,
@@ -1043,6 +1087,7 @@ int nufft_plan_destroy(nufft_plan_t p) {
         cudaSetDevice(p->device);
         cudaDeviceSynchronize();
         destroy_ffts(p);
+        fft1_free(&p->fft1);
         free_pointset(&p->src);
         free_pointset(&p->tgt);
         for (int d = 0; d < 3; ++d) dfree(p->dec[d]);
@@ -1096,6 +1141,7 @@ int nufft_plan_get_info(nufft_plan_t p, nufft_plan_info* info) {
         info->kernel_launches = p->launches;
         info->fft_execs = p->fft_execs;
         info->fft64 = p->fft64 ? 1 : 0;
+        info->fft_own = fft1_wanted(p) ? 1 : 0;
     });
 }
 

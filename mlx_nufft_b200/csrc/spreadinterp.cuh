@@ -820,8 +820,4 @@ inline CellPtrs cell_ptrs(const PointSet& ps) {
     return cp;
 }
 
-// Raise a kernel's dynamic shared-memory limit to `bytes` when it exceeds
-// the 48 KB default (host-side attribute call, cached per kernel).
-void ensure_smem(const void* kernel, size_t bytes);
-
 }  // namespace nufft
