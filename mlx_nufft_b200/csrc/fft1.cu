@@ -34,6 +34,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <mutex>
 #include <set>
 #include <type_traits>
@@ -44,7 +45,14 @@
 namespace nufft {
 namespace {
 
-constexpr int kFftThreads = 256;
+// Threads per CTA and the largest in-register radix.
+#ifndef NUFFT_FFT_THREADS
+#define NUFFT_FFT_THREADS 256
+#endif
+#ifndef NUFFT_FFT_RMAX_LOG2
+#define NUFFT_FFT_RMAX_LOG2 5
+#endif
+constexpr int kFftThreads = NUFFT_FFT_THREADS;
 
 // Columns per CTA at length 2048, and resident CTAs per SM the kernels are
 // compiled for (caps their registers at 128; measured on 2^21 cells: pass 1
@@ -72,7 +80,8 @@ __host__ __device__ constexpr int fft_cols(int L) {
 
 // Radix of the stage that starts at span NS (see the file comment).
 __host__ __device__ constexpr int stage_radix(int L, int NS) {
-    const int k = ilog2(L), st = (k + 4) / 5;
+    constexpr int rb = NUFFT_FFT_RMAX_LOG2;
+    const int k = ilog2(L), st = (k + rb - 1) / rb;
     const int done = ilog2(NS);
     int t = 0, acc = 0;
     while (acc < done) {
@@ -299,6 +308,7 @@ k_fft1_rows(const float2* __restrict__ A, int N1, int n,
             int64_t out_stride, int64_t N, const float* __restrict__ dec) {
     constexpr int C = fft_cols(L);
     extern __shared__ float2 s[];
+    asm volatile("griddepcontrol.wait;" ::: "memory");   // pass 1 has completed
     const int v = blockIdx.y;
     const int r0 = blockIdx.x * C;
     A += (int64_t)v * n;
@@ -387,8 +397,8 @@ void run_rows(const Fft1& f, const float2* A, bool crop, bool inv, float2* out,
         dim3 g((unsigned)(f.N1 / fft_cols(L)), (unsigned)nv);
         auto launch = [&](auto k) {
             prepare((const void*)k, smem);
-            k<<<g, kFftThreads, smem, st>>>(A, f.N1, f.n, f.tw + f.N1, out, out_stride,
-                                            N, dec);
+            launch_dependent(k, g, dim3(kFftThreads), smem, st, A, f.N1, f.n,
+                             (const float2*)(f.tw + f.N1), out, out_stride, N, dec);
         };
         if (crop)
             inv ? launch(k_fft1_rows<L, true, true>) : launch(k_fft1_rows<L, false, true>);
@@ -399,6 +409,14 @@ void run_rows(const Fft1& f, const float2* A, bool crop, bool inv, float2* out,
 }
 
 }  // namespace
+
+bool pdl_on() {
+    static const bool on = [] {
+        const char* e = std::getenv("NUFFT_PDL");
+        return (e && *e) ? std::atoi(e) != 0 : true;
+    }();
+    return on;
+}
 
 bool fft1_supported(int64_t n) {
     return n >= (1 << 12) && n <= (1 << 22) && (n & (n - 1)) == 0;

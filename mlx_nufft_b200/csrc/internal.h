@@ -153,6 +153,31 @@ struct PointSet {
 // the 48 KB default (host-side attribute call, cached per kernel).
 void ensure_smem(const void* kernel, size_t bytes);
 
+// Programmatic dependent launch: a kernel launched this way may be
+// scheduled while the previous kernel in its stream drains; its first
+// action is griddepcontrol.wait (grid_dep_wait), so it touches no memory
+// before that kernel has completed.  NUFFT_PDL=0 launches normally.
+bool pdl_on();
+template <typename... KArgs, typename... Args>
+void launch_dependent(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                      cudaStream_t st, Args... args) {
+    if (!pdl_on()) {
+        k<<<grid, block, smem, st>>>(args...);
+        return;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    check_cuda(cudaLaunchKernelEx(&cfg, k, args...), "cudaLaunchKernelEx");
+}
+
 // Two-pass FFT of a power-of-two 1-D fine grid (fft1.cu), n = N1 * N2.
 struct Fft1 {
     int n = 0, N1 = 0, N2 = 0;   // n == 0: not in use

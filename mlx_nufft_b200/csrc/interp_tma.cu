@@ -363,6 +363,7 @@ k_interp1_stream(const float2* __restrict__ grid, int nvg, int msub,
     __shared__ __align__(8) uint64_t bar[2];
     __shared__ int ring[2];
     __shared__ int s_ok;
+    grid_dep_wait();                  // the FFT that writes `grid` has completed
     const StreamLayout L = stream_layout(tg.tcells, msub, nvg, phase != nullptr);
     const uint64_t pol = l2_evict_last_policy();
     if (threadIdx.x == 0) {
@@ -559,9 +560,10 @@ void interp1_stream_impl(const PointSet& ps, const TileGeom& tg, const float2* g
         const size_t smem = stages * (size_t)L.stage_bytes;
         ensure_smem((const void*)k, smem);
         const int blocks = persistent_grid((const void*)k, smem, ps.nsub, threads);
-        k<<<blocks, threads, smem, st>>>(
-            grid + (int64_t)v0 * tg.ncells, nv, msub, ps.perm, ps.cell[0], ps.phase,
-            ps.subs, (int)ps.nsub, ps.sched, out + v0 * ostride, ostride, tg, err);
+        launch_dependent(k, dim3(blocks), dim3(threads), smem, st,
+                         grid + (int64_t)v0 * tg.ncells, nv, msub, ps.perm, ps.cell[0],
+                         ps.phase, ps.subs, (int)ps.nsub, ps.sched, out + v0 * ostride,
+                         ostride, tg, err);
         NUFFT_LAUNCH("k_interp1_stream");
     }
 }

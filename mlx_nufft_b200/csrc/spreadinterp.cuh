@@ -35,6 +35,12 @@ struct CellPtrs {
     const int2* d[3];
 };
 
+// Wait for the grid this one depends on (programmatic dependent launch;
+// a no-op for a normal launch).
+__device__ __forceinline__ void grid_dep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // Exact ES kernel in fp32 (reference form, kept for checks).
 __device__ __forceinline__ float es_weight(float d, float c2w, float beta) {
     float z = d * c2w;
