@@ -246,7 +246,9 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
     const int m1 = m1d > 0 ? m1d : (interp ? 512 : 1024);
     static const int m3i = env_int("NUFFT_BIN_3D_INTERP", 0);
     const int m3 = interp ? (m3i > 0 ? m3i : 10) : 8;
-    int m0 = dim == 1 ? m1 : (dim == 2 ? 32 : m3);
+    static const int m2d = env_int("NUFFT_BIN_2D", 0);
+    const int m2 = m2d > 0 ? m2d : 32;
+    int m0 = dim == 1 ? m1 : (dim == 2 ? m2 : m3);
     for (int d = 0; d < 3; ++d) {
         if (d < dim) {
             tg.n[d] = (int)n[d];
@@ -301,8 +303,15 @@ int vectors_per_tile(const TileGeom& tg, int nbatch) {
 // Automatic choice: tiled when the tile fits, there are enough points
 // (nd.py:304), and the points per bin on average pay for the per-subproblem
 // tile traffic (one load, or one zero + flush, of the whole tile).  Below
-// that density the global kernels touch only the points' own taps.
-bool want_tiled(const nufft_plan_s* p, int64_t npts, const TileGeom& tg) {
+// that density the global kernels touch only the points' own taps.  A 2-D
+// spread (types 1 and 3 sources) also needs kTiled2dSpreadPerCell points
+// per fine cell: below it the tiled kernel's zero + flush of 38^2-cell
+// tiles costs more than the global atomics (measured on a 512^2 grid:
+// 1e5 points 47 vs 39 us, 3e5 134 vs 104 us; 1e6 243 vs 448 us).
+constexpr double kTiled2dSpreadPerCell = 2.0;
+
+bool want_tiled(const nufft_plan_s* p, int64_t npts, const TileGeom& tg,
+                bool spread) {
     if (p->opts.method == NUFFT_METHOD_GLOBAL) return false;
     const bool fits = tile_fits(tg);
     if (p->opts.method == NUFFT_METHOD_TILED) {
@@ -312,6 +321,9 @@ bool want_tiled(const nufft_plan_s* p, int64_t npts, const TileGeom& tg) {
     static const int min_per_bin = env_int("NUFFT_MIN_PER_BIN", kTiledMinPerBin);
     double bins = 1.0;
     for (int d = 0; d < tg.dim; ++d) bins *= tg.nb[d];
+    if (spread && tg.dim == 2 &&
+        (double)npts < kTiled2dSpreadPerCell * (double)tg.ncells)
+        return false;
     return fits && npts >= kTiledMinPoints && (double)npts >= min_per_bin * bins;
 }
 
@@ -480,7 +492,7 @@ void setpts_t12(nufft_plan_s* p, int64_t M, const double* const* xs,
         cp.m[d] = p->tg_src.m[d];
         cp.nb[d] = p->tg_src.nb[d];
     }
-    const bool tiled = want_tiled(p, M, p->tg_src);
+    const bool tiled = want_tiled(p, M, p->tg_src, p->type == 1);
     const bool sort = tiled || p->opts.sort_points;
     cp.chunk = tiled ? sort_chunk(p->dim) : 0;
     PhaseParams pp{};
@@ -610,7 +622,7 @@ void set_sources_t3(nufft_plan_s* p, int64_t M, const double* const* xs,
     pp.isign = p->isign;
     pp.fp32 = !(prec == NUFFT_PREC_CRIT64 || prec == NUFFT_PREC_PHASES64);
     for (int d = 0; d < p->dim; ++d) pp.D[d] = p->D[d];
-    const bool tiled = want_tiled(p, M, p->tg_src);
+    const bool tiled = want_tiled(p, M, p->tg_src, true);
     const bool sort = tiled || p->opts.sort_points;
     cp.chunk = tiled ? sort_chunk(p->dim) : 0;
     build_pointset(&p->src, cp, M, xs, sort, tiled, kMsubSpread, false, pp,
@@ -672,7 +684,7 @@ void setpts_t3(nufft_plan_s* p, int64_t M, const double* const* xs, int64_t N,
     pp.ftd = p->d_ftd;
     pp.fta = p->d_fta;
     pp.nq = 128;
-    const bool tiled = want_tiled(p, N, p->tg_tgt);
+    const bool tiled = want_tiled(p, N, p->tg_tgt, false);
     const bool sort = tiled || p->opts.sort_points;
     cp.chunk = tiled ? sort_chunk(p->dim) : 0;
     build_pointset(&p->tgt, cp, N, ss, sort, tiled, interp_msub(p->dim), true, pp,

@@ -72,7 +72,7 @@ def test_type2_small(dim, N, isign, eps, method, rng):
 
 
 @pytest.mark.parametrize("dim,N,M", [(1, (4096,), 300_000),
-                                     (2, (256, 200), 300_000),
+                                     (2, (128, 100), 300_000),
                                      (3, (64, 48, 40), 300_000)])
 def test_tiled_auto_large(dim, N, M, rng):
     """P >= 2e4 takes the tiled (bin-sorted) path automatically; check a
@@ -91,6 +91,22 @@ def test_tiled_auto_large(dim, N, M, rng):
     cj = p2.execute(fk)
     idx = rng.choice(M, 200, replace=False)
     assert port.rel_l2(cj[idx], fast.direct_t2(x, fk, -1, idx)) <= gate(1e-6)
+
+
+def test_2d_low_density_spread_global(rng):
+    """A 2-D type-1 plan below 2 points per fine cell (the quickstart's
+    1e5 points on 512^2 cells) spreads with the global kernel; its type-2
+    sibling keeps the tiled interpolation."""
+    from mlx_nufft_b200 import Type1PlanND, Type2PlanND
+    M, N = 100_000, (256, 256)
+    x = pts(rng, 2, M)
+    c = rng.standard_normal(M) + 1j * rng.standard_normal(M)
+    p1 = Type1PlanND(tuple(x), N, eps=1e-6, isign=+1)
+    assert not p1._od
+    f = p1.execute(c).ravel()
+    idx = rng.choice(f.size, 200, replace=False)
+    assert port.rel_l2(f[idx], fast.direct_t1(x, c, N, +1, idx)) <= gate(1e-6)
+    assert Type2PlanND(tuple(x), N, eps=1e-6)._od
 
 
 @pytest.mark.parametrize("dim,N", [(1, (4096,)), (2, (512, 384)),
