@@ -378,7 +378,8 @@ def run_expi(args, cfg, torch, dist, world, rank, local, barrier):
             "roofline": {"bound": "hbm", "achieved": alg / (kern_ms / 1e3) / 1e9,
                          "peak": peak, "unit": "GB/s",
                          "frac": alg / (kern_ms / 1e3) / 1e9 / peak,
-                         "traffic": None, "kernel": "k_expi",
+                         "traffic": ncu_traffic(f"cfg{args.config}"),
+                         "kernel": "k_expi2",
                          "algorithmic_bytes": alg, "peak_kind": peak_kind},
             "e2e": {"value": world * n / (float(e2e_t.item()) / 1e3), "unit": "elem/s",
                     "h2d_bytes_per_step": 8 * n, "d2h_bytes_per_step": 8 * n,

@@ -298,13 +298,7 @@ struct ExpiComps {
     const double* p[kMaxExpiComps];
 };
 
-__global__ void __launch_bounds__(256)
-k_expi(ExpiComps comps, int ncomp, int64_t n, float sgn,
-       float2* __restrict__ out) {
-    const int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (j >= n) return;
-    double phi = 0.0;
-    for (int c = 0; c < ncomp; ++c) phi += __ldg(comps.p[c] + j);
+__device__ __forceinline__ float2 expi_one(double phi, float sgn) {
     const double k = rint(phi * (1.0 / kTwoPi));
     double r = fma(-k, kTwoPi, phi);
     r = fma(-k, kTwoPiLo, r);
@@ -314,7 +308,58 @@ k_expi(ExpiComps comps, int ncomp, int64_t n, float sgn,
     sincosf(hi, &s, &c);
     const float sr = fmaf(c, lo, s);     // sin(hi + lo) to first order
     const float cr = fmaf(-s, lo, c);    // cos(hi + lo) to first order
-    out[j] = make_float2(cr, sgn * sr);
+    return make_float2(cr, sgn * sr);
+}
+
+// E (even) consecutive elements per thread: 16-byte loads per component
+// and 16-byte stores (every component and the output 16-byte aligned); the
+// elements past the last full group run one by one.
+#ifndef NUFFT_EXPI_PER
+#define NUFFT_EXPI_PER 4
+#endif
+constexpr int kExpiPer = NUFFT_EXPI_PER;
+
+__global__ void __launch_bounds__(256)
+k_expi2(ExpiComps comps, int ncomp, int64_t n, float sgn,
+        float2* __restrict__ out) {
+    constexpr int E = kExpiPer;
+    const int64_t j = E * (blockIdx.x * (int64_t)blockDim.x + threadIdx.x);
+    if (j >= n) return;
+    if (j + E <= n) {
+        double phi[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) phi[e] = 0.0;
+        for (int c = 0; c < ncomp; ++c) {
+#pragma unroll
+            for (int e = 0; e < E; e += 2) {
+                const double2 v =
+                    __ldg(reinterpret_cast<const double2*>(comps.p[c] + j + e));
+                phi[e] += v.x;
+                phi[e + 1] += v.y;
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < E; e += 2) {
+            const float2 a = expi_one(phi[e], sgn), b = expi_one(phi[e + 1], sgn);
+            *reinterpret_cast<float4*>(out + j + e) = make_float4(a.x, a.y, b.x, b.y);
+        }
+    } else {
+        for (int64_t i = j; i < n; ++i) {
+            double phi = 0.0;
+            for (int c = 0; c < ncomp; ++c) phi += __ldg(comps.p[c] + i);
+            out[i] = expi_one(phi, sgn);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256)
+k_expi(ExpiComps comps, int ncomp, int64_t n, float sgn,
+       float2* __restrict__ out) {
+    const int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    double phi = 0.0;
+    for (int c = 0; c < ncomp; ++c) phi += __ldg(comps.p[c] + j);
+    out[j] = expi_one(phi, sgn);
 }
 
 void launch_expi(int ncomp, const double* const* comps, int64_t n, int isign,
@@ -324,10 +369,19 @@ void launch_expi(int ncomp, const double* const* comps, int64_t n, int isign,
     if (n <= 0) return;
     ExpiComps cp{};
     for (int c = 0; c < ncomp; ++c) cp.p[c] = comps[c];
-    const int64_t blocks = (n + 255) / 256;
-    k_expi<<<(unsigned)blocks, 256, 0, st>>>(cp, ncomp, n,
-                                             isign >= 0 ? 1.0f : -1.0f, out);
-    NUFFT_LAUNCH("k_expi");
+    const float sgn = isign >= 0 ? 1.0f : -1.0f;
+    bool aligned = (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+    for (int c = 0; c < ncomp; ++c)
+        aligned &= (reinterpret_cast<uintptr_t>(comps[c]) & 15) == 0;
+    if (aligned) {
+        const int64_t blocks = ((n + kExpiPer - 1) / kExpiPer + 255) / 256;
+        k_expi2<<<(unsigned)blocks, 256, 0, st>>>(cp, ncomp, n, sgn, out);
+        NUFFT_LAUNCH("k_expi2");
+    } else {
+        const int64_t blocks = (n + 255) / 256;
+        k_expi<<<(unsigned)blocks, 256, 0, st>>>(cp, ncomp, n, sgn, out);
+        NUFFT_LAUNCH("k_expi");
+    }
 }
 
 }  // namespace nufft

@@ -196,6 +196,23 @@ def test_expi_isign_components_shape(rng):
     assert np.max(np.abs(expi(big, return_np=True) - np.exp(1j * big))) < 1e-5
 
 
+def test_expi_paired_and_unaligned(rng):
+    """Odd lengths (the last element of the two-per-thread kernel alone) and
+    an 8-byte-offset device view (the one-per-thread kernel) give the same
+    bits as the aligned call."""
+    import torch
+    from mlx_nufft_b200 import expi
+    phi = rng.uniform(-1e6, 1e6, 100_001)
+    e = expi(phi, return_np=True)
+    assert np.max(np.abs(e - port.expi_ref(phi))) <= GATE_SMALL
+    dev = torch.from_numpy(phi).cuda()
+    view = dev[1:]                          # data pointer 8 bytes past 16-byte alignment
+    assert view.data_ptr() % 16 == 8
+    e_view = expi(view, return_np=True)
+    assert np.array_equal(e_view, expi(np.ascontiguousarray(phi[1:]), return_np=True))
+    assert np.array_equal(e_view, e[1:])
+
+
 def test_type3_1d_tiled_targets(rng):
     """1-D type 3 with enough targets for the tiled (streamed) interp, whose
     stages carry the targets' post-phases."""
