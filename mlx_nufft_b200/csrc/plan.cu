@@ -243,7 +243,7 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
     tg.keval = keval ? 1 : 0;
     tg.poly = make_es_poly(w, beta);
     static const int m1d = env_int("NUFFT_BIN_1D", 0);
-    const int m1 = m1d > 0 ? m1d : (interp ? 512 : 1024);
+    const int m1 = m1d > 0 ? m1d : 1024;
     static const int m3i = env_int("NUFFT_BIN_3D_INTERP", 0);
     const int m3 = interp ? (m3i > 0 ? m3i : 10) : 8;
     static const int m2d = env_int("NUFFT_BIN_2D", 0);
@@ -274,13 +274,17 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
 // few cells, so the cost that dominates is the caller-ordered access of
 // its strength (spread) or output (interp), which a plain bin sort turns
 // into a random 8-byte scatter/gather over the whole array.  Sorting by
-// (chunk, bin) bounds the array slice in flight to ~16 MB (L2-resident);
-// the price is one extra tile load per bin per chunk, from L2.  In 3-D the
+// (chunk, bin) bounds the array slice in flight to 8-16 MB (L2-resident);
+// the price is one extra tile load per bin per chunk, from L2.  1-D
+// interpolation uses 2^20-point chunks with 1024-cell bins (cfg 2: 0.096 ms
+// vs 0.104 for 2^21 with 512-cell bins, which has as many subproblems;
+// 2048-cell bins with 2^19 0.123); spreading keeps 2^21.  In 3-D the
 // per-point tap work dominates and bins need all their points, so 0.
-// NUFFT_SORT_CHUNK_LOG2 overrides the default (tuning; 0 disables).
-int64_t sort_chunk(int dim) {
-    static const int lg = env_int("NUFFT_SORT_CHUNK_LOG2", 21);
-    return (dim <= 2 && lg > 0) ? (int64_t)1 << lg : 0;
+// NUFFT_SORT_CHUNK_LOG2 overrides the default (tuning; negative disables).
+int64_t sort_chunk(int dim, bool interp) {
+    static const int lg = env_int("NUFFT_SORT_CHUNK_LOG2", 0);
+    const int l = lg > 0 ? lg : (dim == 1 && interp ? 20 : 21);
+    return (dim <= 2 && lg >= 0) ? (int64_t)1 << l : 0;
 }
 
 // dynamic shared memory available to a tile (kernels keep < 1 KB static)
@@ -494,7 +498,7 @@ void setpts_t12(nufft_plan_s* p, int64_t M, const double* const* xs,
     }
     const bool tiled = want_tiled(p, M, p->tg_src, p->type == 1);
     const bool sort = tiled || p->opts.sort_points;
-    cp.chunk = tiled ? sort_chunk(p->dim) : 0;
+    cp.chunk = tiled ? sort_chunk(p->dim, p->type == 2) : 0;
     PhaseParams pp{};
     build_pointset(&p->src, cp, M, xs, sort, tiled,
                    p->type == 1 ? kMsubSpread : interp_msub(p->dim), p->type == 2,
@@ -624,7 +628,7 @@ void set_sources_t3(nufft_plan_s* p, int64_t M, const double* const* xs,
     for (int d = 0; d < p->dim; ++d) pp.D[d] = p->D[d];
     const bool tiled = want_tiled(p, M, p->tg_src, true);
     const bool sort = tiled || p->opts.sort_points;
-    cp.chunk = tiled ? sort_chunk(p->dim) : 0;
+    cp.chunk = tiled ? sort_chunk(p->dim, false) : 0;
     build_pointset(&p->src, cp, M, xs, sort, tiled, kMsubSpread, false, pp,
                    p->d_err, st);
     check_err_flag(p, st);
@@ -686,7 +690,7 @@ void setpts_t3(nufft_plan_s* p, int64_t M, const double* const* xs, int64_t N,
     pp.nq = 128;
     const bool tiled = want_tiled(p, N, p->tg_tgt, false);
     const bool sort = tiled || p->opts.sort_points;
-    cp.chunk = tiled ? sort_chunk(p->dim) : 0;
+    cp.chunk = tiled ? sort_chunk(p->dim, true) : 0;
     build_pointset(&p->tgt, cp, N, ss, sort, tiled, interp_msub(p->dim), true, pp,
                    p->d_err, st);
     check_err_flag(p, st);
