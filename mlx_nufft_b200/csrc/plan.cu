@@ -243,7 +243,9 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
     tg.keval = keval ? 1 : 0;
     tg.poly = make_es_poly(w, beta);
     static const int m1d = env_int("NUFFT_BIN_1D", 0);
-    const int m1 = m1d > 0 ? m1d : 1024;
+    // 1-D interp bins: 1792 cells (cfg 2 interp 0.091 ms; 1024: 0.096,
+    // 1536: 0.092, 2048: 0.105 -- its stages leave 3 CTAs per SM, not 4)
+    const int m1 = m1d > 0 ? m1d : (interp ? 1792 : 1024);
     static const int m3i = env_int("NUFFT_BIN_3D_INTERP", 0);
     const int m3 = interp ? (m3i > 0 ? m3i : 10) : 8;
     static const int m2d = env_int("NUFFT_BIN_2D", 0);
@@ -276,7 +278,7 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
 // into a random 8-byte scatter/gather over the whole array.  Sorting by
 // (chunk, bin) bounds the array slice in flight to 8-16 MB (L2-resident);
 // the price is one extra tile load per bin per chunk, from L2.  1-D
-// interpolation uses 2^20-point chunks with 1024-cell bins (cfg 2: 0.096 ms
+// interpolation uses 2^20-point chunks (cfg 2 with 1024-cell bins: 0.096 ms
 // vs 0.104 for 2^21 with 512-cell bins, which has as many subproblems;
 // 2048-cell bins with 2^19 0.123); spreading keeps 2^21.  In 3-D the
 // per-point tap work dominates and bins need all their points, so 0.
