@@ -101,3 +101,25 @@ def test_fft1_batch_and_disjoint(rng):
         sel = groups == g
         ref = port.nufft_t1([x[sel]], c[sel], (N,), 1e-6, +1)
         assert port.rel_l2(out[g], ref) <= FP32_FLOOR
+
+
+def test_type3_1d_fused_pad(rng):
+    """1-D type 3 with sigma_inner = 2: sources spread onto nf = 2048 cells,
+    padded to a 4096-cell grid by the first FFT pass (the pad reads the
+    spread grid with the type-3 (-1)^q corrections).  At the default
+    sigma_inner = 1.25 no type-3 grid is a power of two."""
+    from oracle import fast
+    from mlx_nufft_b200 import Type3Plan
+    P, M, X, S = 30_000, 40_000, 8.0, 317.3
+    x = rng.uniform(-X, X, P)
+    s = rng.uniform(-S, S, M)
+    x[:2] = (-X, X)                       # pin the extents
+    s[:2] = (-S, S)
+    c = rng.standard_normal(P) + 1j * rng.standard_normal(P)
+    plan = Type3Plan((x,), (s,), eps=1e-5, sigma_inner=2.0)
+    info = plan._plan.info()
+    assert info.fft_own == 1 and info.nf[0] == 2048 and info.n_up[0] == 4096
+    f = plan.execute(c)
+    idx = rng.choice(M, 400, replace=False)
+    exact = fast.direct_sum([x], c, [s], +1, idx)
+    assert port.rel_l2(f[idx], exact) <= gate(1e-5)
