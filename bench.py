@@ -402,8 +402,21 @@ def main():
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+        # NCCL may print its version banner on file descriptor 1 while the
+        # communicator is set up; send that to stderr so that rank 0's
+        # stdout carries only the JSON line
+        sys.stdout.flush()
+        saved_fd = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local))
+            dist.barrier()
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved_fd, 1)
+            os.close(saved_fd)
 
     def barrier():
         if world > 1:
