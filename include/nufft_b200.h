@@ -143,12 +143,30 @@ int nufft_set_sources(nufft_plan_t plan, int64_t M, const double* x,
  * Type 1: in = c[nvec][M], out = f[nvec][N0][N1][N2].
  * Type 2: in = f[nvec][N...], out = c[nvec][M] (caller point order).
  * Type 3: in = c[nvec][M], out = f[nvec][N_tgt] (target order).
- * Asynchronous on `stream`; no host synchronisation.
+ * Asynchronous on `stream`; no host synchronisation.  Device-side failures
+ * (an interpolation tile copy whose bounded wait ran out: that execute's
+ * output is invalid) are recorded in the plan and returned as
+ * NUFFT_ERR_CUDA by the plan's next execute / setpts call, or by
+ * nufft_plan_check.
  * Replaces: Type1PlanND.execute / execute_batch (mlx_nufft/nd.py:581,744),
  * Type2PlanND.execute (nd.py:1075), GpuT3Plan.execute / execute_batch
  * (mlx_nufft/gpu_t3.py:1287,941), Plan.execute (mlx_nufft/api.py:331).     */
 int nufft_execute(nufft_plan_t plan, const void* in, void* out, int nvec,
                   void* stream);
+
+/* Apply the adjoint of the planned transform to `nvec` vectors (device
+ * complex64, vector-major): the sibling transform with the opposite sign.
+ * Type-1 plan: in = f[nvec][N...] (modes), out = c[nvec][M] (points, caller
+ * order).  Type-2 plan: in = c[nvec][M], out = f[nvec][N...].  Type-3 plan:
+ * in = f[nvec][N_tgt] (targets), out = c[nvec][M] (sources).  Types 1/2
+ * reuse the plan's own sorted points, corrections and fine grids (no
+ * second setpts); a type-3 plan builds its sibling plan (targets as
+ * sources, opposite sign) on the first call, from device copies of the
+ * coordinates it keeps since setpts, which makes that first call
+ * synchronise `stream`.  Asynchronous otherwise.
+ * Replaces Plan.execute_adjoint (mlx_nufft/api.py:347-388). */
+int nufft_execute_adjoint(nufft_plan_t plan, const void* in, void* out,
+                          int nvec, void* stream);
 
 /* Types 1 and 2: one stage of nufft_execute on nvec <= n_trans vectors, so
  * a caller can combine the fine grids across GPUs between the stages: sum
@@ -175,6 +193,11 @@ int nufft_execute_disjoint(nufft_plan_t plan, const void* c,
 
 /* Release the plan and every device buffer it owns. */
 int nufft_plan_destroy(nufft_plan_t plan);
+
+/* Synchronise `stream` and report a device-side failure recorded by the
+ * plan's executes so far (NUFFT_ERR_CUDA; the flag is then cleared), else
+ * NUFFT_OK.  No reference counterpart (MLX raises at mx.eval). */
+int nufft_plan_check(nufft_plan_t plan, void* stream);
 
 int nufft_plan_get_info(nufft_plan_t plan, nufft_plan_info* info);
 
@@ -220,11 +243,14 @@ int nufft_expi(int ncomp, const double* const* comps, int64_t n, int isign,
  *   out[j] = sum over the w^dim taps of psi(taps) * grid[(i1 + l) mod n]
  * for the M points (x, y, z) (fp64, folded mod 2*pi onto the grid spacing
  * 2*pi / n_grid[d]), with the ES kernel (w, beta) = nufft_kernel_params(eps,
- * upsampfac) evaluated in its exp/sqrt form.  `grid` is a complex64 fine
- * grid of n_grid[0] x .. x n_grid[dim-1] cells (C order, FFT order) -- e.g.
- * the grid a type-2 plan with the same eps / upsampfac has just
- * transformed (nufft_get_grid); `out` is complex64[M] in caller order.
- * Each n_grid[d] must be in [2w, 2^31).
+ * upsampfac) evaluated in its exp/sqrt form.  `grid` must be a complex64
+ * (interleaved float) fine grid of n_grid[0] x .. x n_grid[dim-1] cells
+ * (C order, FFT order) -- e.g. the grid a type-2 plan with the same eps /
+ * upsampfac has just transformed (nufft_get_grid), but only when that plan
+ * reports nufft_plan_info.fft64 == 0: a plan that runs its FFT in fp64
+ * holds a complex128 grid, which this entry point cannot read (the pointer
+ * carries no type; it would be misread).  `out` is complex64[M] in caller
+ * order.  Each n_grid[d] must be in [2w, 2^31).
  *
  * Scratch: the points' cell indices and fractions (8 bytes per point per
  * dimension) live in one static device array of NUFFT_NOALLOC_SCRATCH_BYTES,
@@ -235,7 +261,9 @@ int nufft_expi(int ncomp, const double* const* comps, int64_t n, int isign,
  * streams, or threads without ordering) race and corrupt each other's
  * results -- order them on one stream.  The first call on each device looks
  * up the array's device address (cudaGetSymbolAddress); make that first call
- * before any stream capture.  Non-finite coordinates are evaluated as 0. */
+ * before any stream capture.  A point with a non-finite coordinate gets the
+ * output NaN + NaN*i (the call itself is asynchronous and cannot return an
+ * error for it; plans reject such points at setpts instead). */
 int nufft_interp_noalloc(int dim, const int64_t* n_grid, double eps,
                          double upsampfac, const void* grid, int64_t M,
                          const double* x, const double* y, const double* z,

@@ -91,6 +91,9 @@ _PROTOS = {
     "nufft_execute": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
         ctypes.c_void_p]),
+    "nufft_execute_adjoint": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+        ctypes.c_void_p]),
     "nufft_execute_stage": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
         ctypes.c_int, ctypes.c_void_p]),
@@ -100,6 +103,7 @@ _PROTOS = {
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
         ctypes.c_void_p, ctypes.c_void_p]),
     "nufft_plan_destroy": (ctypes.c_int, [ctypes.c_void_p]),
+    "nufft_plan_check": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "nufft_plan_get_info": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.POINTER(NufftPlanInfo)]),
     "nufft_get_stage_times": (ctypes.c_int, [

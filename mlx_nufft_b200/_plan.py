@@ -87,6 +87,20 @@ class NativePlan:
             check(lib.nufft_execute(self._h, inp.data_ptr(), out.data_ptr(),
                                     int(nvec), stream_ptr()))
 
+    def execute_adjoint(self, inp, out, nvec):
+        """nufft_execute_adjoint: the sibling transform with the opposite
+        sign on the plan's own points (types 1/2) or on a sibling plan the
+        library builds once (type 3)."""
+        with torch.cuda.device(self.device):
+            check(lib.nufft_execute_adjoint(self._h, inp.data_ptr(), out.data_ptr(),
+                                            int(nvec), stream_ptr()))
+
+    def check(self):
+        """nufft_plan_check: synchronise and raise a device-side failure
+        recorded by earlier executes."""
+        with torch.cuda.device(self.device):
+            check(lib.nufft_plan_check(self._h, stream_ptr()))
+
     def execute_stage(self, stage, inp, out, nvec):
         with torch.cuda.device(self.device):
             check(lib.nufft_execute_stage(

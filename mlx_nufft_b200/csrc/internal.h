@@ -93,6 +93,13 @@ struct CellParams {
     // that chunk's slice of the caller-ordered strengths / outputs, which
     // stays L2-resident while it is being gathered or scattered.
     int64_t chunk;
+    // Interpolation point sets ordered inside each subproblem (cell_order):
+    // the shared-tile strides (cells) of the interpolation kernel that will
+    // read them, per dimension.  Non-zero: points are dealt round-robin over
+    // the 16 residues (sum_d l_d rs[d]) mod 16 of their first tap's tile
+    // index, so the 16 lanes of a half-warp read 16 distinct 8-byte bank
+    // pairs (no shared-memory bank conflicts); zero: plain cell order.
+    int rs[3];
 };
 
 struct TileGeom {
@@ -250,6 +257,8 @@ void launch_spread(const PointSet& ps, const TileGeom& tg, int w,
 // applicable, use launch_interp).
 bool make_grid_tmap(CUtensorMap* map, const float2* grid, const TileGeom& tg,
                     int nbatch);
+// Row stride (cells) of the TMA-staged 3-D tile: T[2] + 1 rounded up to even.
+int tma_box_x(const TileGeom& tg);
 bool launch_interp_tma(const PointSet& ps, const TileGeom& tg, int w,
                        const CUtensorMap* map, const float2* grid, int nvec,
                        float2* out, int64_t ostride, int* err, cudaStream_t st);

@@ -19,8 +19,9 @@
 // by the CTA's threads with wrap, into the same padded layout.
 //
 // Every mbarrier wait is bounded: after kSpinLimit polls the CTA records
-// an error in err[0], waits (bounded again) for its other copy in flight,
-// and stops.
+// an error in *err (the plan's host-mapped execute error flag, which the
+// next call on the plan reports), waits (bounded again) for both of its
+// buffers' copies, and stops.
 #include <cuda.h>
 
 #include <algorithm>
@@ -84,6 +85,15 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map,
         " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_addr(dst)),
         "l"(map), "r"(x), "r"(y), "r"(z), "r"(v), "r"(smem_addr(bar))
         : "memory");
+}
+
+// Record a failed (timed-out) tile copy in the plan's execute error flag.
+// The flag is pinned host memory mapped into the device address space, so
+// the host reads it without a device synchronisation; a plain system-scope
+// store (no atomic over the host link) is enough for a single flag value.
+__device__ __forceinline__ void report_tile_wait(int* err) {
+    *(volatile int*)err = kErrTileWait;
+    __threadfence_system();
 }
 
 struct TmaBin {
@@ -185,12 +195,14 @@ k_interp_tma(const __grid_constant__ CUtensorMap tmap, const float2* __restrict_
     int b = 0;
     uint32_t parity0 = 0u, parity1 = 0u;
     bool failed = false;
+    bool cur_interior = false;
     while (cur < nsub) {
         const int4 sb = subs[cur];
         const TmaBin bn = tma_bin(sb.z, tg, B2, use_tma);
         float2* tile = sbuf + (size_t)b * nvg * TS;
         bool ok = true;
         int xoff;
+        cur_interior = bn.interior;
         if (bn.interior) {
             ok = mbar_wait(&bar[b], b ? parity1 : parity0);
             if (b) parity1 ^= 1u; else parity0 ^= 1u;
@@ -265,9 +277,12 @@ k_interp_tma(const __grid_constant__ CUtensorMap tmap, const float2* __restrict_
         b ^= 1;
     }
     if (failed && threadIdx.x == 0) {
-        atomicOr(err, kErrTileWait);
-        // the other buffer may still have a copy in flight: wait for it
-        // (bounded) before the CTA's shared memory is released
+        report_tile_wait(err);
+        // neither buffer may keep a copy in flight once the CTA's shared
+        // memory is released: wait again (bounded) for the copy whose wait
+        // timed out (buffer b, the phase before the parity flip) and for
+        // the other buffer's
+        if (cur_interior) mbar_wait(&bar[b], (b ? parity1 : parity0) ^ 1u);
         const int o = ring[b ^ 1];
         if (o < nsub && tma_bin(subs[o].z, tg, B2, use_tma).interior)
             mbar_wait(&bar[b ^ 1], b ? parity0 : parity1);
@@ -374,7 +389,7 @@ k_interp1_stream(const float2* __restrict__ grid, int nvg, int msub,
     }
     __syncthreads();
     if (!s_ok) {            // misaligned stage buffers: record and stop
-        if (threadIdx.x == 0) atomicOr(err, kErrTileWait);
+        if (threadIdx.x == 0) report_tile_wait(err);
         scheduler_done(sched);
         return;
     }
@@ -469,8 +484,11 @@ k_interp1_stream(const float2* __restrict__ grid, int nvg, int msub,
         b ^= 1;
     }
     if (failed && threadIdx.x == 0) {
-        atomicOr(err, kErrTileWait);
-        // the other stage may hold a copy in flight: wait for it (bounded)
+        report_tile_wait(err);
+        // no stage may keep a copy in flight once the CTA's shared memory is
+        // released: wait again (bounded) for the stage whose wait timed out
+        // (the phase before the parity flip) and for the other stage
+        mbar_wait(&bar[b], (b ? parity1 : parity0) ^ 1u);
         if (ring[b ^ 1] < nsub) mbar_wait(&bar[b ^ 1], b ? parity0 : parity1);
     }
     scheduler_done(sched);

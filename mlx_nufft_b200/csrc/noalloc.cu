@@ -49,8 +49,9 @@ struct Coords3 {
 };
 
 // crit64 fold of types 1/2 (mod 2pi, / h, ceil(xi - w/2)), the cell index
-// shifted so that i1 + w/2 lies in [0, n).  Non-finite coordinates are
-// evaluated as 0.
+// shifted so that i1 + w/2 lies in [0, n).  A non-finite coordinate gets
+// the cell of 0 (so the interpolation reads inside the grid) and a NaN
+// fraction, which k_noalloc_mark_nonfinite turns into a NaN output.
 __global__ void __launch_bounds__(256)
 k_noalloc_cells(int64_t M, int dim, Coords3 X, int64_t n0, int64_t n1,
                 int64_t n2, double halfw_d, int halfw, int2* cells) {
@@ -59,15 +60,28 @@ k_noalloc_cells(int64_t M, int dim, Coords3 X, int64_t n0, int64_t n1,
     const int64_t n[3] = {n0, n1, n2};
     for (int d = 0; d < dim; ++d) {
         double x = X.p[d][j];
-        if (!isfinite(x)) x = 0.0;
+        const bool bad = !isfinite(x);
+        if (bad) x = 0.0;
         double r = fmod(x, kTwoPi);
         if (r < 0.0) r += kTwoPi;
         const double xi = r / (2.0 * kPi / (double)n[d]);
         const double i1d = ceil(xi - halfw_d);
         int64_t b = ((int64_t)i1d + halfw) % n[d];
         if (b < 0) b += n[d];
-        cells[d * M + j] = make_int2((int)(b - halfw), __float_as_int((float)(xi - i1d)));
+        const float fr = bad ? __int_as_float(0x7fc00000) : (float)(xi - i1d);
+        cells[d * M + j] = make_int2((int)(b - halfw), __float_as_int(fr));
     }
+}
+
+// Points whose fraction was marked NaN above (a non-finite coordinate)
+// get the output NaN + NaN i.
+__global__ void __launch_bounds__(256)
+k_noalloc_mark_nonfinite(int64_t M, int dim, const int2* cells, float2* out) {
+    const int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (j >= M) return;
+    bool bad = false;
+    for (int d = 0; d < dim; ++d) bad |= isnan(__int_as_float(cells[d * M + j].y));
+    if (bad) out[j] = make_float2(__int_as_float(0x7fc00000), __int_as_float(0x7fc00000));
 }
 
 }  // namespace
@@ -136,6 +150,8 @@ extern "C" int nufft_interp_noalloc(int dim, const int64_t* n_grid, double eps,
                 M, tg);
             NUFFT_LAUNCH("k_interp_global (no-alloc)");
         }));
+        k_noalloc_mark_nonfinite<<<blocks, 256, 0, st>>>(M, dim, cells, (float2*)out);
+        NUFFT_LAUNCH("k_noalloc_mark_nonfinite");
         return NUFFT_OK;
     } catch (const Error& e) {
         set_last_error(e.msg);

@@ -148,7 +148,24 @@ struct nufft_plan_s {
     bool profile = false;
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     bool ev_recorded = false;
-    int* d_err = nullptr;
+    int* d_err = nullptr;      // setpts error bits (device memory)
+    // execute error flag: pinned host memory mapped into the device address
+    // space (h_exec_err on the host, d_exec_err for the kernels); an
+    // interpolation kernel whose bounded tile-copy wait ran out stores
+    // kErrTileWait there, and the next call on the plan reports it
+    int* h_exec_err = nullptr;
+    int* d_exec_err = nullptr;
+    // Adjoint (nufft_execute_adjoint).  Types 1/2 run the sibling transform
+    // (the other type, opposite sign) on this plan's own sorted points,
+    // corrections and grids; gadj is the complex64 spreading target of a
+    // type-2 plan's adjoint when its FFT grid is complex128.  Type 3 keeps
+    // device copies of its sources and targets and builds the sibling plan
+    // (targets -> sources, opposite sign) on first use.
+    float2* gadj = nullptr;
+    double* xcopy[3] = {nullptr, nullptr, nullptr};
+    double* scopy[3] = {nullptr, nullptr, nullptr};
+    int64_t xcap = 0, scap = 0;
+    nufft_plan_s* adj = nullptr;
     int64_t launches = 0;      // own kernels launched by executes
     int64_t fft_execs = 0;     // cuFFT executions issued by executes
     // TMA tensor map over the complex64 FFT grids for the 3-D interpolation,
@@ -376,11 +393,12 @@ cufftHandle get_fft(nufft_plan_s* p, int nv) {
     return h;
 }
 
-// In-place FFT of nv fine grids (gfft), unnormalised inverse for isign > 0.
-void run_fft(nufft_plan_s* p, int nv, cudaStream_t st) {
+// In-place FFT of nv fine grids (gfft): the unnormalised inverse when
+// `inv` (a transform of sign +1), else the forward transform.
+void run_fft(nufft_plan_s* p, int nv, bool inv, cudaStream_t st) {
     cufftHandle h = get_fft(p, nv);
     check_cufft(cufftSetStream(h, st), "cufftSetStream");
-    const int dir = p->isign > 0 ? CUFFT_INVERSE : CUFFT_FORWARD;
+    const int dir = inv ? CUFFT_INVERSE : CUFFT_FORWARD;
     ++p->fft_execs;
     if (p->fft64)
         check_cufft(cufftExecZ2Z(h, (cufftDoubleComplex*)p->gfft,
@@ -402,6 +420,8 @@ float2* t1_spread_grid(const nufft_plan_s* p) {
 }
 
 void alloc_grids(nufft_plan_s* p) {
+    dfree(p->gadj);             // re-created at the new batch size on use
+    p->gadj = nullptr;
     dfree(p->gfft);
     p->gfft = nullptr;
     dfree(p->gspread);
@@ -430,6 +450,20 @@ void record(nufft_plan_s* p, int i, cudaStream_t st) {
     if (p->profile) NUFFT_CUDA(cudaEventRecord(p->ev[i], st));
 }
 
+// Report (and clear) a tile-copy timeout that an earlier execute recorded in
+// the plan's host-mapped flag; reading it needs no device synchronisation
+// (a flag raised by an execute still in flight is reported by a later call).
+void check_exec_flag(nufft_plan_s* p) {
+    if (!p->h_exec_err) return;
+    const int h = *(volatile int*)p->h_exec_err;
+    if (h) {
+        *(volatile int*)p->h_exec_err = 0;
+        fail(NUFFT_ERR_CUDA, "an interpolation tile copy of an earlier execute on "
+                             "this plan did not complete; that execute's output is "
+                             "invalid");
+    }
+}
+
 void check_err_flag(nufft_plan_s* p, cudaStream_t st) {
     int h = 0;
     NUFFT_CUDA(cudaMemcpyAsync(&h, p->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
@@ -437,9 +471,6 @@ void check_err_flag(nufft_plan_s* p, cudaStream_t st) {
     if (h) {
         NUFFT_CUDA(cudaMemsetAsync(p->d_err, 0, sizeof(int), st));
         NUFFT_CUDA(cudaStreamSynchronize(st));
-        if (h & kErrTileWait)
-            fail(NUFFT_ERR_CUDA, "an interpolation tile copy did not complete "
-                                 "(earlier execute results are invalid)");
         fail(NUFFT_ERR_ARG, "non-finite nonuniform coordinate");
     }
 }
@@ -484,6 +515,24 @@ void create_t12(nufft_plan_s* p) {
     p->sized = true;
 }
 
+// Shared-tile strides of the interpolation kernel that will read an
+// interpolation point set (CellParams::rs): the 1-D tile is contiguous;
+// the 3-D TMA-staged tile (complex64 grids) has rows of tma_box_x cells,
+// the plain tiled kernel's (complex128 grids) rows of T[2] cells; the 2-D
+// kernel reads cell-unordered points (rs = 0).
+void interp_strides(const nufft_plan_s* p, const TileGeom& tg, CellParams* cp) {
+    static const int tma_on = env_int("NUFFT_INTERP_TMA", 1);
+    cp->rs[0] = cp->rs[1] = cp->rs[2] = 0;
+    if (tg.dim == 1) {
+        cp->rs[0] = 1;
+    } else if (tg.dim == 3) {
+        const int S = (tma_on && !p->fft64) ? tma_box_x(tg) : tg.T[2];
+        cp->rs[0] = tg.T[1] * S;
+        cp->rs[1] = S;
+        cp->rs[2] = 1;
+    }
+}
+
 void setpts_t12(nufft_plan_s* p, int64_t M, const double* const* xs,
                 cudaStream_t st) {
     CellParams cp{};
@@ -501,6 +550,7 @@ void setpts_t12(nufft_plan_s* p, int64_t M, const double* const* xs,
     const bool tiled = want_tiled(p, M, p->tg_src, p->type == 1);
     const bool sort = tiled || p->opts.sort_points;
     cp.chunk = tiled ? sort_chunk(p->dim, p->type == 2) : 0;
+    if (p->type == 2) interp_strides(p, p->tg_src, &cp);
     PhaseParams pp{};
     build_pointset(&p->src, cp, M, xs, sort, tiled,
                    p->type == 1 ? kMsubSpread : interp_msub(p->dim), p->type == 2,
@@ -636,6 +686,27 @@ void set_sources_t3(nufft_plan_s* p, int64_t M, const double* const* xs,
     check_err_flag(p, st);
 }
 
+// Device copies of a type-3 plan's coordinates (for its adjoint), grown
+// when needed; copies on `st`.
+void keep_coords(double** dst, int64_t* cap, int dim, int64_t n,
+                 const double* const* src, cudaStream_t st) {
+    if (n > *cap) {
+        for (int d = 0; d < 3; ++d) {
+            dfree(dst[d]);
+            dst[d] = nullptr;
+        }
+        *cap = 0;
+        for (int d = 0; d < dim; ++d)
+            dst[d] = (double*)dmalloc(sizeof(double) * n, "type-3 coordinates");
+        *cap = n;
+    }
+    for (int d = 0; d < dim; ++d)
+        NUFFT_CUDA(cudaMemcpyAsync(dst[d], src[d], sizeof(double) * n,
+                                   cudaMemcpyDeviceToDevice, st));
+}
+
+void drop_adjoint(nufft_plan_s* p);
+
 void setpts_t3(nufft_plan_s* p, int64_t M, const double* const* xs, int64_t N,
                const double* const* ss, cudaStream_t st) {
     if (N < 1) fail(NUFFT_ERR_ARG, "at least one target is required");
@@ -693,12 +764,16 @@ void setpts_t3(nufft_plan_s* p, int64_t M, const double* const* xs, int64_t N,
     const bool tiled = want_tiled(p, N, p->tg_tgt, false);
     const bool sort = tiled || p->opts.sort_points;
     cp.chunk = tiled ? sort_chunk(p->dim, true) : 0;
+    interp_strides(p, p->tg_tgt, &cp);
     build_pointset(&p->tgt, cp, N, ss, sort, tiled, interp_msub(p->dim), true, pp,
                    p->d_err, st);
     check_err_flag(p, st);
     p->Ntgt = N;
     // sources: guard against the extent only when it was given explicitly
     set_sources_t3(p, M, xs, p->opts.has_source_extent != 0, st);
+    drop_adjoint(p);
+    keep_coords(p->scopy, &p->scap, p->dim, N, ss, st);
+    keep_coords(p->xcopy, &p->xcap, p->dim, M, xs, st);
     p->points_set = true;
 }
 
@@ -767,7 +842,7 @@ void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
             } else {
                 if (p->fft64)
                     launch_widen(sg, (double2*)p->gfft, p->nupcells * nv, st);
-                run_fft(p, nv, st);
+                run_fft(p, nv, inv, st);
                 record(p, 2, st);
                 launch_crop(p->dim, p->N, p->nup, p->dec, p->gfft, p->fft64, out, nv,
                             st);
@@ -785,7 +860,7 @@ void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
                 launch_pad(p->dim, p->N, p->nup, p->dec, in, p->gfft, p->fft64, nv,
                            st);
                 record(p, 1, st);
-                run_fft(p, nv, st);
+                run_fft(p, nv, inv, st);
             }
             record(p, 2, st);
         }
@@ -800,7 +875,7 @@ void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
             record(p, 2, st);
         }
         if (!launch_interp_tma(p->src, p->tg_src, p->w, interp_tmap(p, p->tg_src),
-                               interp_grid32(p), nv, out, p->src.M, p->d_err, st))
+                               interp_grid32(p), nv, out, p->src.M, p->d_exec_err, st))
             launch_interp(p->src, p->tg_src, p->w, p->gfft, p->fft64, nv, out,
                           p->src.M, p->nvg_src, st);
         record(p, 3, st);
@@ -817,16 +892,89 @@ void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
             launch_pad(p->dim, p->nf, p->nup, p->dec, p->gspread, p->gfft, p->fft64,
                        nv, st);
             record(p, 1, st);
-            run_fft(p, nv, st);
+            run_fft(p, nv, inv, st);
         }
         record(p, 2, st);
         if (!launch_interp_tma(p->tgt, p->tg_tgt, p->w2, interp_tmap(p, p->tg_tgt),
-                               interp_grid32(p), nv, out, p->Ntgt, p->d_err, st))
+                               interp_grid32(p), nv, out, p->Ntgt, p->d_exec_err, st))
             launch_interp(p->tgt, p->tg_tgt, p->w2, p->gfft, p->fft64, nv, out,
                           p->Ntgt, p->nvg_tgt, st);
         record(p, 3, st);
     }
     p->ev_recorded = p->profile;
+}
+
+// Adjoint of a type-1 / type-2 plan on nv vectors: the other type with the
+// opposite sign, on the plan's own sorted points, corrections and grids
+// (the reference builds this sibling as a separate plan over the same
+// points, mlx_nufft/api.py:347-388).  A type-1 plan's adjoint maps modes
+// in[nv][N...] to points out[nv][M]; a type-2 plan's maps points
+// in[nv][M] to modes out[nv][N...].
+void adjoint_chunk_t12(nufft_plan_s* p, const float2* in, float2* out, int nv,
+                       cudaStream_t st) {
+    const bool f1 = use_fft1(p);
+    const bool inv = p->isign < 0;             // sign of the adjoint: -isign
+    if (p->type == 1) {
+        if (f1) {
+            fft1_cols(&p->fft1, in, p->N[0], p->dec[0], nv, inv, st);
+            fft1_rows(&p->fft1, p->gfft, 0, nullptr, nv, inv, st);
+        } else {
+            launch_pad(p->dim, p->N, p->nup, p->dec, in, p->gfft, p->fft64, nv, st);
+            run_fft(p, nv, inv, st);
+        }
+        if (!launch_interp_tma(p->src, p->tg_src, p->w, interp_tmap(p, p->tg_src),
+                               interp_grid32(p), nv, out, p->src.M, p->d_exec_err, st))
+            launch_interp(p->src, p->tg_src, p->w, p->gfft, p->fft64, nv, out,
+                          p->src.M, p->nvg_src, st);
+        return;
+    }
+    float2* sg = p->gfft;
+    if (p->fft64) {
+        if (!p->gadj)
+            p->gadj = (float2*)dmalloc(sizeof(float2) * p->nupcells * p->nbatch,
+                                       "adjoint spread grid");
+        sg = p->gadj;
+    }
+    NUFFT_CUDA(cudaMemsetAsync(sg, 0, sizeof(float2) * p->nupcells * nv, st));
+    launch_spread(p->src, p->tg_src, p->w, in, p->src.M, nv, sg, p->nvg_src, st);
+    if (f1) {
+        fft1_cols(&p->fft1, sg, 0, nullptr, nv, inv, st);
+        fft1_rows(&p->fft1, out, p->N[0], p->dec[0], nv, inv, st);
+        return;
+    }
+    if (p->fft64) launch_widen(sg, (double2*)p->gfft, p->nupcells * nv, st);
+    run_fft(p, nv, inv, st);
+    launch_crop(p->dim, p->N, p->nup, p->dec, p->gfft, p->fft64, out, nv, st);
+}
+
+void drop_adjoint(nufft_plan_s* p) {
+    if (p->adj) {
+        nufft_plan_destroy(p->adj);
+        p->adj = nullptr;
+    }
+}
+
+// The type-3 sibling plan: the plan's targets as sources and its sources as
+// targets, opposite sign, the plan's options (gpu_t3 construction of the
+// reference's adjoint, mlx_nufft/api.py:367-372).
+nufft_plan_s* t3_adjoint(nufft_plan_s* p, cudaStream_t st) {
+    if (p->adj) return p->adj;
+    nufft_opts o = p->opts;
+    o.has_source_extent = 0;
+    o.profile = 0;
+    nufft_plan_t q = nullptr;
+    int rc = nufft_plan_create(3, p->dim, nullptr, p->n_trans, p->eps, -p->isign, &o,
+                               p->device, &q);
+    if (rc != NUFFT_OK) fail(rc, "adjoint plan: " + g_last_error);
+    rc = nufft_setpts(q, p->Ntgt, p->scopy[0], p->scopy[1], p->scopy[2], p->src.M,
+                      p->xcopy[0], p->xcopy[1], p->xcopy[2], st);
+    if (rc != NUFFT_OK) {
+        const std::string msg = g_last_error;
+        nufft_plan_destroy(q);
+        fail(rc, "adjoint plan setpts: " + msg);
+    }
+    p->adj = q;
+    return q;
 }
 
 // Grow the number of fine grids held by the plan so that nvec vectors run
@@ -944,6 +1092,10 @@ int nufft_plan_create(int type, int dim, const int64_t* n_modes, int n_trans,
                 for (int i = 0; i < 4; ++i) NUFFT_CUDA(cudaEventCreate(&p->ev[i]));
             p->d_err = (int*)dmalloc(sizeof(int), "error flag");
             NUFFT_CUDA(cudaMemset(p->d_err, 0, sizeof(int)));
+            NUFFT_CUDA(cudaHostAlloc((void**)&p->h_exec_err, sizeof(int),
+                                     cudaHostAllocMapped));
+            *p->h_exec_err = 0;
+            NUFFT_CUDA(cudaHostGetDevicePointer((void**)&p->d_exec_err, p->h_exec_err, 0));
             if (type != 3) {
                 for (int d = 0; d < dim; ++d) p->N[d] = n_modes[d];
                 create_t12(p);
@@ -964,6 +1116,7 @@ int nufft_setpts(nufft_plan_t p, int64_t M, const double* x, const double* y,
     return guarded([&] {
         if (!p) fail(NUFFT_ERR_ARG, "NULL plan");
         DeviceGuard g(p->device);
+        check_exec_flag(p);
         cudaStream_t st = (cudaStream_t)stream;
         const double* xs[3] = {x, y, z};
         for (int d = 0; d < p->dim; ++d)
@@ -993,6 +1146,8 @@ int nufft_set_sources(nufft_plan_t p, int64_t M, const double* x,
         } else {
             if (!p->points_set) fail(NUFFT_ERR_STATE, "setpts() must be called first");
             set_sources_t3(p, M, xs, true, st);
+            drop_adjoint(p);
+            keep_coords(p->xcopy, &p->xcap, p->dim, M, xs, st);
         }
     });
 }
@@ -1014,6 +1169,7 @@ int nufft_execute_stage(nufft_plan_t p, int stage, const void* in, void* out,
         if ((stage == NUFFT_STAGE_ALL || stage == NUFFT_STAGE_FINISH) && !out)
             fail(NUFFT_ERR_ARG, "NULL output pointer");
         DeviceGuard g(p->device);
+        check_exec_flag(p);
         cudaStream_t st = (cudaStream_t)stream;
         if (stage == NUFFT_STAGE_ALL) ensure_batch(p, nvec);
         const float2* fin = (const float2*)in;
@@ -1039,6 +1195,42 @@ int nufft_execute(nufft_plan_t p, const void* in, void* out, int nvec,
         return NUFFT_ERR_ARG;
     }
     return nufft_execute_stage(p, NUFFT_STAGE_ALL, in, out, nvec, stream);
+}
+
+int nufft_execute_adjoint(nufft_plan_t p, const void* in, void* out, int nvec,
+                          void* stream) {
+    return guarded([&] {
+        if (!p) fail(NUFFT_ERR_ARG, "NULL plan");
+        if (!p->points_set)
+            fail(NUFFT_ERR_STATE, "setpts() must be called before execute_adjoint()");
+        if (nvec < 1) fail(NUFFT_ERR_ARG, "nvec must be >= 1");
+        if (!in || !out) fail(NUFFT_ERR_ARG, "NULL data pointer");
+        DeviceGuard g(p->device);
+        check_exec_flag(p);
+        cudaStream_t st = (cudaStream_t)stream;
+        const int64_t l0 = launch_count;
+        struct Count {
+            nufft_plan_s* p; int64_t l0;
+            ~Count() { p->launches += launch_count - l0; }
+        } count{p, l0};
+        if (p->type == 3) {
+            nufft_plan_s* q = t3_adjoint(p, st);
+            const int rc = nufft_execute(q, in, out, nvec, stream);
+            if (rc != NUFFT_OK) fail(rc, g_last_error);
+            return;
+        }
+        ensure_batch(p, nvec);
+        // adjoint input / output lengths: type 1 modes -> points, type 2
+        // points -> modes
+        const int64_t il = p->type == 1 ? p->K : p->src.M;
+        const int64_t ol = p->type == 1 ? p->src.M : p->K;
+        const float2* fin = (const float2*)in;
+        float2* fout = (float2*)out;
+        for (int v0 = 0; v0 < nvec; v0 += p->nbatch) {
+            const int nv = std::min(p->nbatch, nvec - v0);
+            adjoint_chunk_t12(p, fin + v0 * il, fout + v0 * ol, nv, st);
+        }
+    });
 }
 
 int nufft_get_grid(nufft_plan_t p, void** grid, int64_t* n_complex) {
@@ -1081,7 +1273,7 @@ int nufft_execute_disjoint(nufft_plan_t p, const void* c, const int32_t* groups,
                     continue;
                 }
                 if (p->fft64) launch_widen(sg, (double2*)p->gfft, p->nupcells * ng, st);
-                run_fft(p, ng, st);
+                run_fft(p, ng, p->isign > 0, st);
                 launch_crop(p->dim, p->N, p->nup, p->dec, p->gfft, p->fft64,
                             fo + (int64_t)g0 * p->K, ng, st);
             }
@@ -1114,10 +1306,26 @@ int nufft_plan_destroy(nufft_plan_t p) {
         dfree(p->d_ftd);
         dfree(p->d_fta);
         dfree(p->d_err);
+        if (p->h_exec_err) cudaFreeHost(p->h_exec_err);
+        dfree(p->gadj);
+        for (int d = 0; d < 3; ++d) {
+            dfree(p->xcopy[d]);
+            dfree(p->scopy[d]);
+        }
+        drop_adjoint(p);
         for (int i = 0; i < 4; ++i)
             if (p->ev[i]) cudaEventDestroy(p->ev[i]);
         cudaSetDevice(cur);
         delete p;
+    });
+}
+
+int nufft_plan_check(nufft_plan_t p, void* stream) {
+    return guarded([&] {
+        if (!p) fail(NUFFT_ERR_ARG, "NULL plan");
+        DeviceGuard g(p->device);
+        NUFFT_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+        check_exec_flag(p);
     });
 }
 

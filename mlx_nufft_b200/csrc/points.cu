@@ -201,15 +201,27 @@ __global__ void k_sub_fill(const uint32_t* count, const uint32_t* start,
 }
 
 // Order the points of every subproblem by their cell inside the bin
-// (row-major, last dimension fastest, the tile's memory order), so that a
-// warp's taps fall on neighbouring shared-memory words instead of random
-// banks.  One CTA per subproblem: shared histogram over the bin's cells
-// with per-point ranks, block-wide exclusive scan, scatter of cells and
-// permutation into the output arrays (same segment of the sorted order).
-// Shared memory: (cells per bin + msub) x 4 bytes.
+// (row-major, last dimension fastest, the tile's memory order), and -- when
+// cp.rs is set -- deal them round-robin over the 16 bank residues of their
+// first tap in the interpolation kernel's shared tile.  One CTA per
+// subproblem:
+//  1. shared histogram over the bin's cells with per-point ranks and a
+//     block-wide exclusive scan give each point its cell-order position c;
+//  2. (interleave) residue r = (sum_d l_d rs[d]) mod 16 of the point's
+//     tile index; k = rank of the point among the residue-r points in cell
+//     order (a ballot multi-split over the cell-ordered residues);
+//  3. the output position is the rank of (k, r) in lexicographic order:
+//     sum_{r'} min(n_{r'}, k) + #{r' < r : n_{r'} > k}, n_r the residue
+//     counts -- so every run of 16 consecutive points (a half-warp of the
+//     interpolation kernels, one point per lane) holds 16 distinct residues
+//     wherever the buckets allow, and the lanes' 8-byte tap loads hit 16
+//     distinct bank pairs;
+// then scatter of cells and permutation into the output arrays (same
+// segment of the sorted order).  Shared memory: (cells per bin + msub
+// [+ msub with the interleave]) x 4 bytes.
 template <int DIM>
 __global__ void __launch_bounds__(256)
-k_sub_sort(const int4* __restrict__ subs, CellParams cp, int mcells,
+k_sub_sort(const int4* __restrict__ subs, CellParams cp, int mcells, int msub,
            const int2* __restrict__ i0, const int2* __restrict__ i1,
            const int2* __restrict__ i2, const uint32_t* __restrict__ pin,
            int2* __restrict__ o0, int2* __restrict__ o1, int2* __restrict__ o2,
@@ -217,7 +229,11 @@ k_sub_sort(const int4* __restrict__ subs, CellParams cp, int mcells,
     extern __shared__ uint32_t sm[];
     uint32_t* hist = sm;              // mcells counters, then starts
     uint32_t* slot = sm + mcells;     // per point: local cell | rank << 16
+    uint32_t* kres = slot + msub;     // per cell-order position: r | k << 4
     __shared__ uint32_t warp_tot[8];
+    __shared__ uint32_t rcount[16];
+    __shared__ uint32_t wres[8][16];
+    const bool inter = cp.rs[0] != 0 || cp.rs[1] != 0 || cp.rs[2] != 0;
     const int4 sb = subs[blockIdx.x];
     const int start = sb.x, cnt = sb.y;
     int o[3] = {0, 0, 0};
@@ -231,6 +247,7 @@ k_sub_sort(const int4* __restrict__ subs, CellParams cp, int mcells,
     }
     const int2* in[3] = {i0, i1, i2};
     for (int q = threadIdx.x; q < mcells; q += blockDim.x) hist[q] = 0u;
+    if (threadIdx.x < 16) rcount[threadIdx.x] = 0u;
     __syncthreads();
     for (int t = threadIdx.x; t < cnt; t += blockDim.x) {
         uint32_t loc = 0;
@@ -267,12 +284,70 @@ k_sub_sort(const int4* __restrict__ subs, CellParams cp, int mcells,
     }
     __syncthreads();
     int2* out[3] = {o0, o1, o2};
+    if (!inter) {
+        for (int t = threadIdx.x; t < cnt; t += blockDim.x) {
+            const uint32_t sl = slot[t];
+            const int pos = start + (int)(hist[sl & 0xffffu] + (sl >> 16));
+#pragma unroll
+            for (int d = 0; d < DIM; ++d) out[d][pos] = in[d][start + t];
+            pout[pos] = pin[start + t];
+        }
+        return;
+    }
+    // 2. cell-order position c of every point and its residue at c
     for (int t = threadIdx.x; t < cnt; t += blockDim.x) {
         const uint32_t sl = slot[t];
-        const int pos = start + (int)(hist[sl & 0xffffu] + (sl >> 16));
+        const uint32_t c = hist[sl & 0xffffu] + (sl >> 16);
+        int tix = 0;
 #pragma unroll
-        for (int d = 0; d < DIM; ++d) out[d][pos] = in[d][start + t];
-        pout[pos] = pin[start + t];
+        for (int d = 0; d < DIM; ++d) {
+            int l = in[d][start + t].x - o[d];
+            l = min(max(l, 0), cp.m[d] - 1);
+            tix += l * cp.rs[d];
+        }
+        kres[c] = (uint32_t)tix & 15u;
+        slot[t] = c;
+    }
+    __syncthreads();
+    //    rank k among the same-residue points, in cell order, 256 at a time
+    for (int base = 0; base < cnt; base += blockDim.x) {
+        if (threadIdx.x < 128) wres[threadIdx.x >> 4][threadIdx.x & 15] = 0u;
+        __syncthreads();
+        const int pe = base + threadIdx.x;
+        const bool act = pe < cnt;
+        const uint32_t r = act ? kres[pe] : 16u;          // 16: no residue
+        const unsigned mask = __match_any_sync(0xffffffffu, r);
+        const uint32_t below = (uint32_t)__popc(mask & ((1u << lane) - 1u));
+        if (act && below == 0) wres[wid][r] = (uint32_t)__popc(mask);
+        __syncthreads();
+        if (act) {
+            uint32_t k = rcount[r] + below;
+            for (int w = 0; w < wid; ++w) k += wres[w][r];
+            kres[pe] = r | (k << 4);
+        }
+        __syncthreads();
+        if (threadIdx.x < 16) {
+            uint32_t s = 0;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) s += wres[w][threadIdx.x];
+            rcount[threadIdx.x] += s;
+        }
+        __syncthreads();
+    }
+    // 3. position = rank of (k, r) in lexicographic order
+    for (int t = threadIdx.x; t < cnt; t += blockDim.x) {
+        const uint32_t kr = kres[slot[t]];
+        const uint32_t r = kr & 15u, k = kr >> 4;
+        uint32_t pos = 0;
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+            const uint32_t n = rcount[q];
+            pos += min(n, k) + ((uint32_t)q < r && n > k ? 1u : 0u);
+        }
+        const int g = start + (int)pos;
+#pragma unroll
+        for (int d = 0; d < DIM; ++d) out[d][g] = in[d][start + t];
+        pout[g] = pin[start + t];
     }
 }
 
@@ -414,17 +489,24 @@ void free_pointset(PointSet* ps) {
 namespace {
 
 // Cell order inside every subproblem (k_sub_sort) into fresh arrays, which
-// then replace the point set's cells and permutation.
+// then replace the point set's cells and permutation.  NUFFT_SUB_SORT
+// (tuning): 0 off, 1 plain cell order, 2 (default) residue interleave when
+// the plan gave the tile strides.
 template <int DIM>
 void sub_sort(PointSet* ps, const CellParams& cp, int msub, cudaStream_t st) {
-    static const char* env = std::getenv("NUFFT_SUB_SORT");  // 0: off (tuning)
-    if (env && *env && std::atoi(env) == 0) return;
+    static const char* env = std::getenv("NUFFT_SUB_SORT");
+    const int mode = (env && *env) ? std::atoi(env) : 2;
+    if (mode == 0) return;
+    CellParams c2 = cp;
+    if (mode == 1) c2.rs[0] = c2.rs[1] = c2.rs[2] = 0;
+    const bool inter = c2.rs[0] != 0 || c2.rs[1] != 0 || c2.rs[2] != 0;
     int mcells = 1;
     for (int d = 0; d < DIM; ++d) mcells *= cp.m[d];
     if (mcells > 65536 || msub > 65536) return;   // 16-bit slot fields
-    const size_t smem = sizeof(uint32_t) * ((size_t)mcells + (size_t)msub);
-    // opt in beyond the default dynamic limit (the kernel also has a few
-    // bytes of static shared memory)
+    const size_t smem = sizeof(uint32_t) *
+                        ((size_t)mcells + (size_t)msub * (inter ? 2 : 1));
+    // opt in beyond the default dynamic limit (the kernel also has about
+    // 0.6 KB of static shared memory)
     if (smem > 40 * 1024) {
         NUFFT_CUDA(cudaFuncSetAttribute((const void*)k_sub_sort<DIM>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -438,7 +520,7 @@ void sub_sort(PointSet* ps, const CellParams& cp, int msub, cudaStream_t st) {
         ps->perm_alt = (uint32_t*)dmalloc(4 * (ps->cap + kPointSlack), "sorted permutation");
     }
     k_sub_sort<DIM><<<(unsigned)ps->nsub, 256, smem, st>>>(
-        ps->subs, cp, mcells, ps->cell[0], ps->cell[1], ps->cell[2], ps->perm,
+        ps->subs, c2, mcells, msub, ps->cell[0], ps->cell[1], ps->cell[2], ps->perm,
         ps->cell_alt[0], ps->cell_alt[1], ps->cell_alt[2], ps->perm_alt);
     NUFFT_LAUNCH("k_sub_sort");
     for (int d = 0; d < DIM; ++d) std::swap(ps->cell[d], ps->cell_alt[d]);
