@@ -101,8 +101,9 @@ typedef struct nufft_plan_info {
     int64_t kernel_launches;       /* this library's kernels launched by executes    */
     int64_t fft_execs;             /* cuFFT executions issued by executes            */
     int     fft64;                 /* 1 if the fine-grid FFT runs in fp64            */
-    int     fft_own;               /* 1 if this library's two-pass 1-D FFT (pad /
-                                      crop fused) replaces pad + cuFFT (+ crop)      */
+    int     fft_own;               /* 1 if this library's own FFT (two-pass 1-D,
+                                      or pruned three-pass 3-D; pad / crop fused)
+                                      replaces pad + cuFFT (+ crop)                  */
 } nufft_plan_info;
 
 /* Fill `opts` with the defaults above. */

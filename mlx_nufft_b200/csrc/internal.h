@@ -205,6 +205,27 @@ void fft1_cols(Fft1* f, const float2* in, int64_t N, const float* dec, int nv,
 void fft1_rows(Fft1* f, float2* out, int64_t N, const float* dec, int nv, bool inv,
                cudaStream_t st);
 
+// Pruned three-pass FFT of a 3-D power-of-two fine grid (each n_d in
+// [64, 2048]) with the pad (types 2) or crop (type 1) fused (fft1.cu).
+struct Fftn {
+    int n[3] = {0, 0, 0};        // fine grid (n[0] == 0: not in use)
+    int N[3] = {0, 0, 0};        // mode box
+    float2* tw = nullptr;        // W_{n_d} tables, d = 0, 1, 2
+    float2* tmp = nullptr;       // scratch B[m0][y][z], tmp_batch grids
+    int tmp_batch = 0;
+};
+bool fftn_supported(const int64_t* n);
+void fftn_init(Fftn* f, const int64_t* n, const int64_t* N);
+void fftn_free(Fftn* f);
+int64_t fftn_scratch_cells(const Fftn& f);
+// nv mode boxes (times the corrections dec[d]) -> nv transformed fine grids
+void fftn_pad(Fftn* f, const float2* modes, const float* const* dec, float2* grid,
+              int nv, bool inv, cudaStream_t st);
+// nv fine grids -> nv mode boxes of the transform times dec[d]; the grids are
+// overwritten (used as scratch)
+void fftn_crop(Fftn* f, float2* grid, const float* const* dec, float2* modes, int nv,
+               bool inv, cudaStream_t st);
+
 // CTAs for a persistent launch of `kernel` (256 threads, `smem` bytes):
 // resident CTAs per SM x SMs, capped at `work` items.
 int persistent_grid(const void* kernel, size_t smem, int64_t work,

@@ -25,6 +25,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "spreadinterp.cuh"
@@ -94,6 +95,39 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map,
 __device__ __forceinline__ void report_tile_wait(int* err) {
     *(volatile int*)err = kErrTileWait;
     __threadfence_system();
+}
+
+// Load a tile that wraps around the periodic grid into the padded tile
+// layout (rows of S cells, vector buffers TS cells apart) with `nthr`
+// threads (thread `tid`): K independent loads in flight per thread before
+// their stores, so the loop is bound by bandwidth, not by one load latency
+// per cell.
+__device__ __forceinline__ void load_wrapped_tile(float2* tile, const float2* grid,
+                                                  const int* o, const TileGeom& tg,
+                                                  int S, int TS, int v0, int nvg,
+                                                  int tid, int nthr) {
+    constexpr int K = 4;
+    for (int v = 0; v < nvg; ++v) {
+        const float2* gv = grid + (int64_t)(v0 + v) * tg.ncells;
+        for (int q0 = tid; q0 < tg.tcells; q0 += K * nthr) {
+            float2 val[K];
+            int sq[K];
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                const int q = q0 + k * nthr;
+                sq[k] = -1;
+                if (q < tg.tcells) {
+                    const int64_t g = tile_to_global<3>(q, o, tg);
+                    const int row = (int)__umulhi((unsigned)q, tg.tdiv[2]);
+                    sq[k] = row * S + (q - row * tg.T[2]);
+                    val[k] = __ldg(gv + g);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < K; ++k)
+                if (sq[k] >= 0) tile[v * TS + sq[k]] = val[k];
+        }
+    }
 }
 
 struct TmaBin {
@@ -210,13 +244,8 @@ k_interp_tma(const __grid_constant__ CUtensorMap tmap, const float2* __restrict_
         } else {
             // wrapped tile (uniform across the CTA): per-thread loads into
             // the same padded layout
-            for (int q = threadIdx.x; q < tg.tcells; q += blockDim.x) {
-                const int64_t g = tile_to_global<3>(q, bn.o, tg);
-                const int row = (int)__umulhi((unsigned)q, tg.tdiv[2]);
-                const int sq = row * S + (q - row * tg.T[2]);
-                for (int v = 0; v < nvg; ++v)
-                    tile[v * TS + sq] = grid[(int64_t)(v0 + v) * tg.ncells + g];
-            }
+            load_wrapped_tile(tile, grid, bn.o, tg, S, TS, v0, nvg, threadIdx.x,
+                              blockDim.x);
             __syncthreads();
             xoff = 0;
         }

@@ -145,6 +145,7 @@ struct nufft_plan_s {
     float2* gfft = nullptr;
     std::map<int, cufftHandle> ffts;
     Fft1 fft1;                 // two-pass 1-D FFT (fft1.cu), when in use
+    Fftn fftn;                 // pruned 3-D FFT with pad / crop (fft1.cu)
     bool profile = false;
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     bool ev_recorded = false;
@@ -247,7 +248,8 @@ void plane_tap_order(TileGeom& tg, int w) {
 // next to its points; smaller stages leave room for more CTAs), 32 x 32 in 2-D,
 // 8 x 8 x 8 in 3-D for spreading (room for several vectors' tiles) and
 // 10 x 10 x 10 for 3-D interpolation (more points per subproblem, less halo:
-// measured 21-27 % faster than 8^3 on the 3-D BASELINE configs).
+// measured 21-27 % faster than 8^3 on the 3-D benchmark workloads: 3-D
+// type 2 at 5e7 clustered points and 3-D type 3 at 1e6 -> 1e6).
 TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
                    bool interp) {
     TileGeom tg{};
@@ -816,6 +818,23 @@ bool use_fft1(nufft_plan_s* p) {
     return true;
 }
 
+// The pruned 3-D FFT of fft1.cu with the pad / crop fused replaces pad +
+// cuFFT (type 2) and cuFFT + crop (type 1) for complex64 3-D grids whose
+// sides are powers of two in [64, 2048] (NUFFT_FFTN=0 keeps cuFFT, for
+// tuning).
+bool fftn_wanted(const nufft_plan_s* p) {
+    static const int on = env_int("NUFFT_FFTN", 1);
+    return on && p->type != 3 && p->dim == 3 && !p->fft64 && fftn_supported(p->nup);
+}
+
+bool use_fftn(nufft_plan_s* p) {
+    if (!fftn_wanted(p)) return false;
+    if (p->fftn.n[0] != p->nup[0] || p->fftn.n[1] != p->nup[1] ||
+        p->fftn.n[2] != p->nup[2])
+        fftn_init(&p->fftn, p->nup, p->N);
+    return true;
+}
+
 void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
                    int stage, cudaStream_t st) {
     const bool f1 = use_fft1(p);
@@ -839,6 +858,10 @@ void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
                 record(p, 2, st);
                 fft1_rows(&p->fft1, out, p->N[0], p->dec[0], nv, inv, st);
                 record(p, 3, st);
+            } else if (use_fftn(p)) {  // pruned FFT with the crop fused
+                fftn_crop(&p->fftn, sg, p->dec, out, nv, inv, st);
+                record(p, 2, st);
+                record(p, 3, st);
             } else {
                 if (p->fft64)
                     launch_widen(sg, (double2*)p->gfft, p->nupcells * nv, st);
@@ -856,6 +879,9 @@ void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
                 fft1_cols(&p->fft1, in, p->N[0], p->dec[0], nv, inv, st);
                 record(p, 1, st);
                 fft1_rows(&p->fft1, p->gfft, 0, nullptr, nv, inv, st);
+            } else if (use_fftn(p)) {  // pruned FFT with the pad fused
+                record(p, 1, st);
+                fftn_pad(&p->fftn, in, p->dec, p->gfft, nv, inv, st);
             } else {
                 launch_pad(p->dim, p->N, p->nup, p->dec, in, p->gfft, p->fft64, nv,
                            st);
@@ -918,6 +944,8 @@ void adjoint_chunk_t12(nufft_plan_s* p, const float2* in, float2* out, int nv,
         if (f1) {
             fft1_cols(&p->fft1, in, p->N[0], p->dec[0], nv, inv, st);
             fft1_rows(&p->fft1, p->gfft, 0, nullptr, nv, inv, st);
+        } else if (use_fftn(p)) {
+            fftn_pad(&p->fftn, in, p->dec, p->gfft, nv, inv, st);
         } else {
             launch_pad(p->dim, p->N, p->nup, p->dec, in, p->gfft, p->fft64, nv, st);
             run_fft(p, nv, inv, st);
@@ -940,6 +968,10 @@ void adjoint_chunk_t12(nufft_plan_s* p, const float2* in, float2* out, int nv,
     if (f1) {
         fft1_cols(&p->fft1, sg, 0, nullptr, nv, inv, st);
         fft1_rows(&p->fft1, out, p->N[0], p->dec[0], nv, inv, st);
+        return;
+    }
+    if (use_fftn(p)) {
+        fftn_crop(&p->fftn, sg, p->dec, out, nv, inv, st);
         return;
     }
     if (p->fft64) launch_widen(sg, (double2*)p->gfft, p->nupcells * nv, st);
@@ -988,6 +1020,8 @@ void ensure_batch(nufft_plan_s* p, int nvec) {
     if (p->type == 3) per += sizeof(float2) * (size_t)p->nfcells;
     else if (p->type == 1 && p->fft64) per += sizeof(float2) * (size_t)p->nupcells;
     if (fft1_wanted(p)) per += sizeof(float2) * (size_t)p->nupcells;  // FFT scratch
+    if (fftn_wanted(p))
+        per += sizeof(float2) * (size_t)(p->N[0] * p->nup[1] * p->nup[2]);
     const size_t have = per * (size_t)p->nbatch;
     const int64_t cap = (int64_t)((free_b / 2 + have) / per);
     const int nb = (int)std::min<int64_t>(nvec, std::max<int64_t>(cap, p->nbatch));
@@ -1266,6 +1300,11 @@ int nufft_execute_disjoint(nufft_plan_t p, const void* c, const int32_t* groups,
                 // labels relative to this window; out-of-window -> -1
                 window_labels(groups, p->src.M, g0, ng, shifted, st);
                 launch_spread_groups(p->src, p->tg_src, p->w, fc, shifted, sg, st);
+                if (use_fftn(p)) {
+                    fftn_crop(&p->fftn, sg, p->dec, fo + (int64_t)g0 * p->K, ng,
+                              p->isign > 0, st);
+                    continue;
+                }
                 if (use_fft1(p)) {
                     fft1_cols(&p->fft1, sg, 0, nullptr, ng, p->isign > 0, st);
                     fft1_rows(&p->fft1, fo + (int64_t)g0 * p->K, p->N[0], p->dec[0], ng,
@@ -1298,6 +1337,7 @@ int nufft_plan_destroy(nufft_plan_t p) {
         cudaDeviceSynchronize();
         destroy_ffts(p);
         fft1_free(&p->fft1);
+        fftn_free(&p->fftn);
         free_pointset(&p->src);
         free_pointset(&p->tgt);
         for (int d = 0; d < 3; ++d) dfree(p->dec[d]);
@@ -1367,7 +1407,7 @@ int nufft_plan_get_info(nufft_plan_t p, nufft_plan_info* info) {
         info->kernel_launches = p->launches;
         info->fft_execs = p->fft_execs;
         info->fft64 = p->fft64 ? 1 : 0;
-        info->fft_own = fft1_wanted(p) ? 1 : 0;
+        info->fft_own = (fft1_wanted(p) || fftn_wanted(p)) ? 1 : 0;
     });
 }
 

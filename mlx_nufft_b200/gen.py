@@ -2,7 +2,7 @@
 
 uniform_points / gen_generic / gen_anisotropic restate the reference's
 harness generators (harness/gen.py:15-90) so benchmarks and parity tests
-draw the same kind of inputs; `config(k)` builds the five BASELINE
+draw the same kind of inputs; `config(k)` builds the five benchmark
 workloads (cfg 1..5, plus the standalone expi input for cfg 5) with their
 stated shapes, distributions and seeds.  `scale` shrinks the point counts
 for quick runs without changing anything else.
@@ -83,7 +83,7 @@ CONFIG_NAMES = {
 
 
 def config(k, scale=1.0, seed=0):
-    """BASELINE workload k (1..5; 6 = the standalone expi of cfg 5; 7..12 =
+    """Benchmark workload k (1..5; 6 = the standalone expi of cfg 5; 7..12 =
     the reference's type-3 paper suite, PAPER_T3).
 
     Returns a dict with keys: type, dim, eps, isign, x (list of fp64

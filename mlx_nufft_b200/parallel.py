@@ -8,8 +8,9 @@ Only the partitions the transforms have naturally are provided:
   n_trans vectors through one plan over the shared points; no collective
   during execute (`vector_range`, `ShardedBatch`);
 * type 2 split by target point -- every rank interpolates its own points
-  from the same fine grid, which one rank computes (pad/deconvolve + FFT)
-  and broadcasts (`Type2TargetSplit`);
+  from the same fine grid, which every rank computes from its copy of the
+  modes (replicate, no collective) or one rank computes (pad/deconvolve +
+  FFT) and broadcasts (`Type2TargetSplit`);
 * type 1 split by point -- every rank spreads its own points onto a full
   fine grid, the grids are summed with one all-reduce, and every rank (or
   one root) finishes with FFT + deconvolution (`Type1PointSplit`);
@@ -161,25 +162,29 @@ class Type1PointSplit:
 
 
 class Type2TargetSplit:
-    """Type 2 with the target points split across the ranks of `group`:
-    `root` computes the fine grid (pad/deconvolve + FFT) once and broadcasts
-    it; every rank interpolates its own points.  `gather=True` assembles the
-    caller-order output of all points (each rank holding the split_range
-    share of the global point list) on every rank."""
+    """Type 2 with the target points split across the ranks of `group`;
+    every rank interpolates its own points from the same fine grid.  With
+    `replicate=True` every rank builds the grid (pad/deconvolve + FFT) from
+    its own copy of the modes, with no collective; otherwise `root` builds
+    it once and broadcasts it (modes held by one rank).  `gather=True`
+    assembles the caller-order output of all points (each rank holding the
+    split_range share of the global point list) on every rank."""
 
-    def __init__(self, stages, n_points_total=None, group=None, root=0):
+    def __init__(self, stages, n_points_total=None, group=None, root=0,
+                 replicate=False):
         self.stages = stages
         self.group = group
         self.root = root
         self.n_total = n_points_total
+        self.replicate = replicate
 
     def execute(self, fk, return_np=True, gather=False):
         rank, world = _world(self.group)
-        if world == 1 or rank == self.root:
+        if world == 1 or rank == self.root or self.replicate:
             g = self.stages.first(fk)
         else:
             g = self.stages.grid()
-        if world > 1:
+        if world > 1 and not self.replicate:
             dist.broadcast(_real(g), src=self.root, group=self.group)
         out = self.stages.second()
         if gather:

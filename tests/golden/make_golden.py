@@ -3,7 +3,7 @@ code (martinlachaine/mlx-nufft v0.1.3).
 
 Run in the build container, where the reference checkout is available:
 
-    python tests/golden/make_golden.py [path-to-reference]
+    python tests/golden/make_golden.py <path-to-reference-checkout>
 
 The reference package imports MLX in mlx_nufft/__init__.py, which is not
 installable here; its numpy-only modules (mlx_nufft/sizing.py,
@@ -178,7 +178,10 @@ def make_gen(gen):
 
 
 def main():
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path of the "
+                 "mlx-nufft v0.1.3 source tree>")
+    root = sys.argv[1]
     sizing, ref_t3, gen = load_reference(root)
     make_sizing(sizing)
     make_gen(gen)

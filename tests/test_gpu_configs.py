@@ -1,4 +1,4 @@
-"""The five BASELINE workloads on the GPU: every config at its full size,
+"""The five benchmark workloads on the GPU: every config at its full size,
 checked against the exact fp64 direct sum on a random output subset (the
 reference's subset-oracle protocol, harness/run_acceptance.py:86-97), plus
 size-independent properties at full size (linearity, repeatability)."""
@@ -43,6 +43,65 @@ def test_cfg2_1d_type2_full():
     f2 = cfg["data"] * (0.5 - 1.5j)
     c2 = plan.execute(f2)
     assert port.rel_l2(c2, c * (0.5 - 1.5j)) < 1e-6
+
+
+def test_cfg2_every_output_vs_fp64_restatement():
+    """All 1e7 outputs of the 1-D type-2 workload against the fp64 CPU
+    restatement of the reference pipeline (oracle/port.py: deconvolve, pad,
+    FFT, fold, interp in fp64) -- rel-L2 2e-5, the fp32 pipeline floor --
+    and the largest pointwise error against the output scale."""
+    from mlx_nufft_b200 import Type2PlanND
+    cfg = gen.config(2)
+    plan = Type2PlanND(tuple(cfg["x"]), cfg["n_modes"], eps=1e-6, isign=-1)
+    c = plan.execute(cfg["data"])
+    ref = port.nufft_t2(cfg["x"], cfg["data"], 1e-6, -1)
+    assert c.shape == ref.shape == (10_000_000,)
+    assert port.rel_l2(c, ref) <= 2e-5
+    assert np.max(np.abs(c - ref)) <= 2e-4 * np.sqrt(np.mean(np.abs(ref) ** 2))
+
+
+def _port_grid_t2(f, N, eps, isign):
+    """The fp64 fine grid of the CPU restatement (deconvolve + pad + FFT),
+    FFT on all host threads."""
+    import os
+    import scipy.fft as sf
+    w, beta, nup = port.fine_grid_sizes(N, eps)
+    g = np.asarray(f, dtype=np.complex128)
+    for d in range(len(N)):
+        k = np.arange(-(N[d] // 2), N[d] - N[d] // 2, dtype=np.float64)
+        dec = 1.0 / port.kernel_ft(2.0 * np.pi * k / nup[d], beta, w)
+        g = g * dec.reshape((1,) * d + (-1,) + (1,) * (len(N) - d - 1))
+    H = np.zeros(nup, dtype=np.complex128)
+    H[np.ix_(*[port._band(N[d], nup[d]) for d in range(len(N))])] = g
+    workers = os.cpu_count() or 1
+    V = (sf.ifftn(H, workers=workers) * H.size if isign > 0
+         else sf.fftn(H, workers=workers))
+    return V, w, beta, nup
+
+
+def test_cfg4_subset_vs_fp64_restatement():
+    """2e5 outputs of the clustered 3-D type-2 workload (half from the
+    uniform half, half from the cluster) against the fp64 CPU restatement
+    interpolating the same points from its own fp64 grid."""
+    from mlx_nufft_b200 import Type2PlanND
+    cfg = gen.config(4)
+    plan = Type2PlanND(tuple(cfg["x"]), cfg["n_modes"], eps=1e-6, isign=-1)
+    c = plan.execute(cfg["data"])
+    del plan
+    V, w, beta, nup = _port_grid_t2(cfg["data"], cfg["n_modes"], 1e-6, -1)
+    rng = np.random.default_rng(44)
+    M = c.size
+    idx = np.concatenate([rng.choice(M // 2, 100_000, replace=False),
+                          M // 2 + rng.choice(M - M // 2, 100_000, replace=False)])
+    i1s, frs = [], []
+    for d in range(3):
+        i1, fr64, _ = port.cells_fold(cfg["x"][d][idx], nup[d], w)
+        i1s.append(i1)
+        frs.append(fr64)
+    ref = port.interp(V, i1s, frs, w, beta, chunk=8192)
+    assert port.rel_l2(c[idx], ref) <= 2e-5
+    assert port.rel_l2(c[idx[:100_000]], ref[:100_000]) <= 2e-5   # uniform half
+    assert port.rel_l2(c[idx[100_000:]], ref[100_000:]) <= 2e-5   # cluster
 
 
 def test_cfg3_3d_type1_batch_full():

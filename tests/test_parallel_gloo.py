@@ -133,16 +133,22 @@ def _worker(rank, world, port_, case, queue):
             root = 0 if case == "t1_root" else None
             r = par.Type1PointSplit(st, root=root).execute(c[lo:hi])
             out = None if r is None else np.asarray(r)
-        elif case == "t2":
+        elif case in ("t2", "t2_replicate"):
             M, N = 2500, (16, 18)
             x = _points(3, M, 2)
             rng = np.random.default_rng(4)
             f = rng.standard_normal(N) + 1j * rng.standard_normal(N)
             lo, hi = par.split_range(M, rank, world)
             st = OracleT2Stages([v[lo:hi] for v in x], N, EPS, -1)
-            # only the root's modes matter: the others pass garbage
-            mine = f if rank == 0 else np.full(N, np.nan)
-            out = np.asarray(par.Type2TargetSplit(st, M).execute(mine, gather=True))
+            if case == "t2":
+                # only the root's modes matter: the others pass garbage
+                mine = f if rank == 0 else np.full(N, np.nan)
+                split = par.Type2TargetSplit(st, M)
+            else:
+                # every rank holds the modes and builds its own grid
+                mine = f
+                split = par.Type2TargetSplit(st, M, replicate=True)
+            out = np.asarray(split.execute(mine, gather=True))
         elif case == "batch":
             M, N, B = 800, (12,), 5
             x = _points(5, M, 1)
@@ -197,8 +203,9 @@ def test_type1_point_split_allreduce(case):
         assert port.rel_l2(res[0], ref) <= TOL and res[1] is None
 
 
-def test_type2_target_split_broadcast():
-    res = _run("t2")
+@pytest.mark.parametrize("case", ["t2", "t2_replicate"])
+def test_type2_target_split(case):
+    res = _run(case)
     M, N = 2500, (16, 18)
     x = _points(3, M, 2)
     rng = np.random.default_rng(4)
