@@ -178,17 +178,18 @@ __device__ __forceinline__ void dft_reg(float2 (&v)[R]) {
     }
 }
 
-// Stockham stages NS, NS*R, ... of a length-L FFT over the CTA's C =
-// fft_cols(L) columns.  The first stage takes its inputs from load(c, i)
+// Stockham stages NS, NS*R, ... of a length-L FFT over the CTA's C columns
+// (fft_stages: C = fft_cols(L)).  SMEM_IO: the input is already in s (the
+// inter-stage layout) and the output is left there in natural order (the
+// caller loads and stores coalesced rows around the call).  The first stage takes its inputs from load(c, i)
 // (row i of column c); the last hands each butterfly's outputs to
 // store(c, base, stride, v): v[r] is row base + r * stride of column c.
 // In between, element (i, c) lives at s[fpad(i * C + c)].  twL[m] = W_L^m
 // (global, read through L1).
-template <int L, int NS, bool INV, class Load, class Store>
-__device__ __forceinline__ void fft_stages(float2* s, const float2* __restrict__ twL,
-                                           const Load& load, const Store& store) {
+template <int L, int NS, bool INV, int C, bool SMEM_IO = false, class Load, class Store>
+__device__ __forceinline__ void fft_stages_c(float2* s, const float2* __restrict__ twL,
+                                             const Load& load, const Store& store) {
     if constexpr (NS < L) {
-        constexpr int C = fft_cols(L);
         constexpr int R = stage_radix(L, NS);
         constexpr bool LAST = NS * R == L;
         constexpr int NB = (L / R) * C;                 // butterflies
@@ -201,8 +202,8 @@ __device__ __forceinline__ void fft_stages(float2* s, const float2* __restrict__
                 const int c = bid % C, j = bid / C;
 #pragma unroll
                 for (int r = 0; r < R; ++r)
-                    v[t][r] = NS == 1 ? load(c, j + r * (L / R))
-                                      : s[fpad((j + r * (L / R)) * C + c)];
+                    v[t][r] = (NS == 1 && !SMEM_IO) ? load(c, j + r * (L / R))
+                                                    : s[fpad((j + r * (L / R)) * C + c)];
                 if (NS > 1) {
                     const int k = j % NS;
 #pragma unroll
@@ -216,16 +217,24 @@ __device__ __forceinline__ void fft_stages(float2* s, const float2* __restrict__
             }
         }
         if constexpr (LAST) {
+            if (SMEM_IO) __syncthreads();              // all reads of s done
 #pragma unroll
             for (int t = 0; t < PER; ++t) {
                 const int bid = threadIdx.x + t * kFftThreads;
                 if (NB % kFftThreads == 0 || bid < NB) {
                     const int c = bid % C, j = bid / C;
-                    store(c, (j / NS) * NS * R + (j % NS), NS, v[t]);
+                    const int base = (j / NS) * NS * R + (j % NS);
+                    if constexpr (SMEM_IO) {
+#pragma unroll
+                        for (int r = 0; r < R; ++r)
+                            s[fpad((base + r * NS) * C + c)] = v[t][r];
+                    } else {
+                        store(c, base, NS, v[t]);
+                    }
                 }
             }
         } else {
-            if (NS > 1) __syncthreads();               // all reads of s done
+            if (NS > 1 || SMEM_IO) __syncthreads();    // all reads of s done
 #pragma unroll
             for (int t = 0; t < PER; ++t) {
                 const int bid = threadIdx.x + t * kFftThreads;
@@ -238,9 +247,15 @@ __device__ __forceinline__ void fft_stages(float2* s, const float2* __restrict__
                 }
             }
             __syncthreads();
-            fft_stages<L, NS * R, INV>(s, twL, load, store);
+            fft_stages_c<L, NS * R, INV, C, SMEM_IO>(s, twL, load, store);
         }
     }
+}
+
+template <int L, int NS, bool INV, class Load, class Store>
+__device__ __forceinline__ void fft_stages(float2* s, const float2* __restrict__ twL,
+                                           const Load& load, const Store& store) {
+    fft_stages_c<L, NS, INV, fft_cols(L)>(s, twL, load, store);
 }
 
 // Inter-pass twiddles are taken exactly from the tables every kTwExact
@@ -437,6 +452,25 @@ void run_rows(const Fft1& f, const float2* A, bool crop, bool inv, float2* out,
 // Columns of the Y and X passes are C adjacent z-cells, so every access is
 // a contiguous C x 8-byte segment.
 
+// Columns per CTA of the 3-D passes: 16 up to length 512 (every load and
+// store of the Y / X passes a 128-byte row segment, and every thread busy
+// in the first stage), as the 1-D passes above that.
+__host__ __device__ constexpr int fftn_cols(int L) {
+    return L <= 512 ? 16 : fft_cols(L);
+}
+
+template <int L>
+size_t fftn_smem() {
+    constexpr int cells = L * fftn_cols(L) + ((L * fftn_cols(L)) >> 4);
+    return sizeof(float2) * (size_t)cells;
+}
+
+// Resident CTAs per SM the 3-D passes are compiled for (caps registers at
+// 85; measured 0.85 vs 1.00 ms for the pad passes of a 512^3 grid at 2).
+#ifndef NUFFT_FFTN_MINB
+#define NUFFT_FFTN_MINB 3
+#endif
+
 __device__ __forceinline__ int band_mode(int i, int n, int N) {
     // mode index m (0..N-1) of fine cell i, or -1 outside the mode box
     const int m = (i >= n - N / 2 ? i - n : i) + N / 2;
@@ -448,45 +482,67 @@ __device__ __forceinline__ constexpr int vals_len() {
     return std::extent<std::remove_reference_t<V>>::value;
 }
 
-// pass Z of the pad: rows r = m0 * N1 + m1 of the mode box
+// pass Z of the pad: rows r = m0 * N1 + m1 of the mode box.  The CTA's C
+// rows are contiguous in both the modes and A, so they move through shared
+// memory: coalesced loads of the in-band modes (times the corrections)
+// into the transform's layout, the FFT in place, coalesced stores of whole
+// rows.
 template <int L, bool INV>
-__global__ void __launch_bounds__(kFftThreads, NUFFT_FFT_MINB_COLS)
+__global__ void __launch_bounds__(kFftThreads, NUFFT_FFTN_MINB)
 k_fftn_pad_z(const float2* __restrict__ f, int64_t f_vs, const float* __restrict__ d0,
              const float* __restrict__ d1, const float* __restrict__ d2, int N1,
              int N2, int nrows, const float2* __restrict__ twL,
              float2* __restrict__ A, int64_t A_vs) {
-    constexpr int C = fft_cols(L);
+    constexpr int C = fftn_cols(L);
     extern __shared__ float2 s[];
     const int r0 = blockIdx.x * C;
-    f += blockIdx.y * f_vs;
-    A += blockIdx.y * A_vs;
-    auto load = [&](int c, int i) {
-        const int r = r0 + c;
-        const int m = band_mode(i, L, N2);
-        float2 x = make_float2(0.0f, 0.0f);
-        if (r < nrows && m >= 0) {
-            const float d = __ldg(d0 + r / N1) * __ldg(d1 + r % N1) * __ldg(d2 + m);
-            const float2 g = __ldg(f + (int64_t)r * N2 + m);
-            x = make_float2(g.x * d, g.y * d);
-        }
-        return x;
-    };
-    auto store = [&](int c, int base, int stride, auto& vals) {
-        const int r = r0 + c;
-        if (r >= nrows) return;
+    const int rows = min(C, nrows - r0);
+    f += blockIdx.y * f_vs + (int64_t)r0 * N2;
+    A += blockIdx.y * A_vs + (int64_t)r0 * L;
+    // K loads in flight per thread before their shared stores
+    constexpr int K = 8;
+    for (int q0 = threadIdx.x; q0 < C * N2; q0 += K * kFftThreads) {
+        float2 x[K];
+        int dst[K];
 #pragma unroll
-        for (int k = 0; k < vals_len<decltype(vals)>(); ++k)
-            A[(int64_t)r * L + base + k * stride] = vals[k];
-    };
-    fft_stages<L, 1, INV>(s, twL, load, store);
+        for (int k = 0; k < K; ++k) {
+            const int q = q0 + k * kFftThreads;
+            const int c = q / N2, m = q - c * N2;
+            // mode m = k + N2/2 sits at fine cell k mod L
+            dst[k] = q < C * N2 ? fpad(((m - N2 / 2 + L) % L) * C + c) : -1;
+            x[k] = make_float2(0.0f, 0.0f);
+            if (q < C * N2 && c < rows) {
+                const int r = r0 + c;
+                const float d = __ldg(d0 + r / N1) * __ldg(d1 + r % N1) * __ldg(d2 + m);
+                const float2 g = __ldg(f + q);
+                x[k] = make_float2(g.x * d, g.y * d);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < K; ++k)
+            if (dst[k] >= 0) s[dst[k]] = x[k];
+    }
+    for (int q = threadIdx.x; q < C * (L - N2); q += kFftThreads) {
+        const int c = q % C, i = N2 - N2 / 2 + q / C;     // out-of-band fine cells
+        s[fpad(i * C + c)] = make_float2(0.0f, 0.0f);
+    }
+    __syncthreads();
+    auto none = [](int, int) { return make_float2(0.0f, 0.0f); };
+    auto nost = [](int, int, int, auto&) {};
+    fft_stages_c<L, 1, INV, C, true>(s, twL, none, nost);
+    __syncthreads();
+    for (int q = threadIdx.x; q < rows * L; q += kFftThreads) {
+        const int c = q / L, i = q - c * L;
+        A[q] = s[fpad(i * C + c)];
+    }
 }
 
 // pass Y of the pad: columns (m0, z0 + c); blockIdx.y = m0
 template <int L, bool INV>
-__global__ void __launch_bounds__(kFftThreads, NUFFT_FFT_MINB_COLS)
+__global__ void __launch_bounds__(kFftThreads, NUFFT_FFTN_MINB)
 k_fftn_pad_y(const float2* __restrict__ A, int64_t A_vs, int N1, int n2,
              const float2* __restrict__ twL, float2* __restrict__ B, int64_t B_vs) {
-    constexpr int C = fft_cols(L);
+    constexpr int C = fftn_cols(L);
     extern __shared__ float2 s[];
     grid_dep_sync();
     const int z0 = blockIdx.x * C;
@@ -502,15 +558,15 @@ k_fftn_pad_y(const float2* __restrict__ A, int64_t A_vs, int N1, int n2,
         for (int k = 0; k < vals_len<decltype(vals)>(); ++k)
             B[(m0 * L + base + k * stride) * n2 + z0 + c] = vals[k];
     };
-    fft_stages<L, 1, INV>(s, twL, load, store);
+    fft_stages_c<L, 1, INV, C>(s, twL, load, store);
 }
 
 // pass X of the pad: columns (y, z0 + c); blockIdx.y = y
 template <int L, bool INV>
-__global__ void __launch_bounds__(kFftThreads, NUFFT_FFT_MINB_COLS)
+__global__ void __launch_bounds__(kFftThreads, NUFFT_FFTN_MINB)
 k_fftn_pad_x(const float2* __restrict__ B, int64_t B_vs, int N0, int n1, int n2,
              const float2* __restrict__ twL, float2* __restrict__ G, int64_t G_vs) {
-    constexpr int C = fft_cols(L);
+    constexpr int C = fftn_cols(L);
     extern __shared__ float2 s[];
     grid_dep_sync();
     const int z0 = blockIdx.x * C;
@@ -527,15 +583,15 @@ k_fftn_pad_x(const float2* __restrict__ B, int64_t B_vs, int N0, int n1, int n2,
         for (int k = 0; k < vals_len<decltype(vals)>(); ++k)
             G[((int64_t)(base + k * stride) * n1 + y) * n2 + z0 + c] = vals[k];
     };
-    fft_stages<L, 1, INV>(s, twL, load, store);
+    fft_stages_c<L, 1, INV, C>(s, twL, load, store);
 }
 
 // pass X of the crop: columns (y, z0 + c) of the full grid, in-band x only
 template <int L, bool INV>
-__global__ void __launch_bounds__(kFftThreads, NUFFT_FFT_MINB_COLS)
+__global__ void __launch_bounds__(kFftThreads, NUFFT_FFTN_MINB)
 k_fftn_crop_x(const float2* __restrict__ G, int64_t G_vs, int N0, int n1, int n2,
               const float2* __restrict__ twL, float2* __restrict__ B, int64_t B_vs) {
-    constexpr int C = fft_cols(L);
+    constexpr int C = fftn_cols(L);
     extern __shared__ float2 s[];
     const int z0 = blockIdx.x * C;
     const int64_t y = blockIdx.y;
@@ -551,15 +607,15 @@ k_fftn_crop_x(const float2* __restrict__ G, int64_t G_vs, int N0, int n1, int n2
             if (m >= 0) B[((int64_t)m * n1 + y) * n2 + z0 + c] = vals[k];
         }
     };
-    fft_stages<L, 1, INV>(s, twL, load, store);
+    fft_stages_c<L, 1, INV, C>(s, twL, load, store);
 }
 
 // pass Y of the crop: columns (m0, z0 + c), in-band y only
 template <int L, bool INV>
-__global__ void __launch_bounds__(kFftThreads, NUFFT_FFT_MINB_COLS)
+__global__ void __launch_bounds__(kFftThreads, NUFFT_FFTN_MINB)
 k_fftn_crop_y(const float2* __restrict__ B, int64_t B_vs, int N1, int n2,
               const float2* __restrict__ twL, float2* __restrict__ A, int64_t A_vs) {
-    constexpr int C = fft_cols(L);
+    constexpr int C = fftn_cols(L);
     extern __shared__ float2 s[];
     grid_dep_sync();
     const int z0 = blockIdx.x * C;
@@ -576,41 +632,52 @@ k_fftn_crop_y(const float2* __restrict__ B, int64_t B_vs, int N1, int n2,
             if (m >= 0) A[(m0 * N1 + m) * n2 + z0 + c] = vals[k];
         }
     };
-    fft_stages<L, 1, INV>(s, twL, load, store);
+    fft_stages_c<L, 1, INV, C>(s, twL, load, store);
 }
 
 // pass Z of the crop: rows r = m0 * N1 + m1, in-band z only, times the
-// deconvolution
+// deconvolution.  Rows are contiguous in A and in the modes: coalesced
+// loads into shared memory, the FFT in place, coalesced stores of the
+// in-band cells.
 template <int L, bool INV>
-__global__ void __launch_bounds__(kFftThreads, NUFFT_FFT_MINB_COLS)
+__global__ void __launch_bounds__(kFftThreads, NUFFT_FFTN_MINB)
 k_fftn_crop_z(const float2* __restrict__ A, int64_t A_vs, const float* __restrict__ d0,
               const float* __restrict__ d1, const float* __restrict__ d2, int N1,
               int N2, int nrows, const float2* __restrict__ twL,
               float2* __restrict__ f, int64_t f_vs) {
-    constexpr int C = fft_cols(L);
+    constexpr int C = fftn_cols(L);
     extern __shared__ float2 s[];
     grid_dep_sync();
     const int r0 = blockIdx.x * C;
-    A += blockIdx.y * A_vs;
-    f += blockIdx.y * f_vs;
-    auto load = [&](int c, int i) {
-        const int r = r0 + c;
-        return r < nrows ? __ldg(A + (int64_t)r * L + i) : make_float2(0.0f, 0.0f);
-    };
-    auto store = [&](int c, int base, int stride, auto& vals) {
-        const int r = r0 + c;
-        if (r >= nrows) return;
-        const float d01 = __ldg(d0 + r / N1) * __ldg(d1 + r % N1);
+    const int rows = min(C, nrows - r0);
+    A += blockIdx.y * A_vs + (int64_t)r0 * L;
+    f += blockIdx.y * f_vs + (int64_t)r0 * N2;
+    constexpr int K = 8;             // loads in flight per thread
+    for (int q0 = threadIdx.x; q0 < C * L; q0 += K * kFftThreads) {
+        float2 x[K];
 #pragma unroll
-        for (int k = 0; k < vals_len<decltype(vals)>(); ++k) {
-            const int m = band_mode(base + k * stride, L, N2);
-            if (m >= 0) {
-                const float d = d01 * __ldg(d2 + m);
-                f[(int64_t)r * N2 + m] = make_float2(vals[k].x * d, vals[k].y * d);
-            }
+        for (int k = 0; k < K; ++k) {
+            const int q = q0 + k * kFftThreads;
+            x[k] = (q < C * L && q / L < rows) ? __ldg(A + q) : make_float2(0.0f, 0.0f);
         }
-    };
-    fft_stages<L, 1, INV>(s, twL, load, store);
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            const int q = q0 + k * kFftThreads;
+            if (q < C * L) s[fpad((q % L) * C + q / L)] = x[k];
+        }
+    }
+    __syncthreads();
+    auto none = [](int, int) { return make_float2(0.0f, 0.0f); };
+    auto nost = [](int, int, int, auto&) {};
+    fft_stages_c<L, 1, INV, C, true>(s, twL, none, nost);
+    __syncthreads();
+    for (int q = threadIdx.x; q < rows * N2; q += kFftThreads) {
+        const int c = q / N2, m = q - c * N2;
+        const int r = r0 + c;
+        const float d = __ldg(d0 + r / N1) * __ldg(d1 + r % N1) * __ldg(d2 + m);
+        const float2 x = s[fpad(((m - N2 / 2 + L) % L) * C + c)];
+        f[q] = make_float2(x.x * d, x.y * d);
+    }
 }
 
 // W_L^m tables (fp64 rounded once to fp32, forward sign) for L = n_d
@@ -704,26 +771,26 @@ void fftn_pad(Fftn* f, const float2* modes, const float* const* dec, float2* gri
         float2* Gv = grid + v0 * G;
         NUFFT_FFT_LEN_SWITCH(n2, {
             const int nrows = N0 * N1;
-            dim3 g((unsigned)((nrows + fft_cols(L) - 1) / fft_cols(L)), (unsigned)k);
-            if (inv) fftn_launch(k_fftn_pad_z<L, true>, g, fft_smem<L>(), st, false, fv, K,
+            dim3 g((unsigned)((nrows + fftn_cols(L) - 1) / fftn_cols(L)), (unsigned)k);
+            if (inv) fftn_launch(k_fftn_pad_z<L, true>, g, fftn_smem<L>(), st, false, fv, K,
                                  dec[0], dec[1], dec[2], N1, N2, nrows, fftn_tw(*f, 2), Av, G);
-            else fftn_launch(k_fftn_pad_z<L, false>, g, fft_smem<L>(), st, false, fv, K,
+            else fftn_launch(k_fftn_pad_z<L, false>, g, fftn_smem<L>(), st, false, fv, K,
                              dec[0], dec[1], dec[2], N1, N2, nrows, fftn_tw(*f, 2), Av, G);
         });
         NUFFT_LAUNCH("k_fftn_pad_z");
         NUFFT_FFT_LEN_SWITCH(n1, {
-            dim3 g((unsigned)(n2 / fft_cols(L)), (unsigned)N0, (unsigned)k);
-            if (inv) fftn_launch(k_fftn_pad_y<L, true>, g, fft_smem<L>(), st, true,
+            dim3 g((unsigned)(n2 / fftn_cols(L)), (unsigned)N0, (unsigned)k);
+            if (inv) fftn_launch(k_fftn_pad_y<L, true>, g, fftn_smem<L>(), st, true,
                                  (const float2*)Av, G, N1, n2, fftn_tw(*f, 1), Bv, Bs);
-            else fftn_launch(k_fftn_pad_y<L, false>, g, fft_smem<L>(), st, true,
+            else fftn_launch(k_fftn_pad_y<L, false>, g, fftn_smem<L>(), st, true,
                              (const float2*)Av, G, N1, n2, fftn_tw(*f, 1), Bv, Bs);
         });
         NUFFT_LAUNCH("k_fftn_pad_y");
         NUFFT_FFT_LEN_SWITCH(n0, {
-            dim3 g((unsigned)(n2 / fft_cols(L)), (unsigned)n1, (unsigned)k);
-            if (inv) fftn_launch(k_fftn_pad_x<L, true>, g, fft_smem<L>(), st, true,
+            dim3 g((unsigned)(n2 / fftn_cols(L)), (unsigned)n1, (unsigned)k);
+            if (inv) fftn_launch(k_fftn_pad_x<L, true>, g, fftn_smem<L>(), st, true,
                                  (const float2*)Bv, Bs, N0, n1, n2, fftn_tw(*f, 0), Gv, G);
-            else fftn_launch(k_fftn_pad_x<L, false>, g, fft_smem<L>(), st, true,
+            else fftn_launch(k_fftn_pad_x<L, false>, g, fftn_smem<L>(), st, true,
                              (const float2*)Bv, Bs, N0, n1, n2, fftn_tw(*f, 0), Gv, G);
         });
         NUFFT_LAUNCH("k_fftn_pad_x");
@@ -744,28 +811,28 @@ void fftn_crop(Fftn* f, float2* grid, const float* const* dec, float2* modes, in
         float2* Av = Gv;         // A'[m0][m1][z] in the grid's memory, dead after pass X
         float2* fv = modes + v0 * K;
         NUFFT_FFT_LEN_SWITCH(n0, {
-            dim3 g((unsigned)(n2 / fft_cols(L)), (unsigned)n1, (unsigned)k);
-            if (inv) fftn_launch(k_fftn_crop_x<L, true>, g, fft_smem<L>(), st, false,
+            dim3 g((unsigned)(n2 / fftn_cols(L)), (unsigned)n1, (unsigned)k);
+            if (inv) fftn_launch(k_fftn_crop_x<L, true>, g, fftn_smem<L>(), st, false,
                                  (const float2*)Gv, G, N0, n1, n2, fftn_tw(*f, 0), Bv, Bs);
-            else fftn_launch(k_fftn_crop_x<L, false>, g, fft_smem<L>(), st, false,
+            else fftn_launch(k_fftn_crop_x<L, false>, g, fftn_smem<L>(), st, false,
                              (const float2*)Gv, G, N0, n1, n2, fftn_tw(*f, 0), Bv, Bs);
         });
         NUFFT_LAUNCH("k_fftn_crop_x");
         NUFFT_FFT_LEN_SWITCH(n1, {
-            dim3 g((unsigned)(n2 / fft_cols(L)), (unsigned)N0, (unsigned)k);
-            if (inv) fftn_launch(k_fftn_crop_y<L, true>, g, fft_smem<L>(), st, true,
+            dim3 g((unsigned)(n2 / fftn_cols(L)), (unsigned)N0, (unsigned)k);
+            if (inv) fftn_launch(k_fftn_crop_y<L, true>, g, fftn_smem<L>(), st, true,
                                  (const float2*)Bv, Bs, N1, n2, fftn_tw(*f, 1), Av, G);
-            else fftn_launch(k_fftn_crop_y<L, false>, g, fft_smem<L>(), st, true,
+            else fftn_launch(k_fftn_crop_y<L, false>, g, fftn_smem<L>(), st, true,
                              (const float2*)Bv, Bs, N1, n2, fftn_tw(*f, 1), Av, G);
         });
         NUFFT_LAUNCH("k_fftn_crop_y");
         NUFFT_FFT_LEN_SWITCH(n2, {
             const int nrows = N0 * N1;
-            dim3 g((unsigned)((nrows + fft_cols(L) - 1) / fft_cols(L)), (unsigned)k);
-            if (inv) fftn_launch(k_fftn_crop_z<L, true>, g, fft_smem<L>(), st, true,
+            dim3 g((unsigned)((nrows + fftn_cols(L) - 1) / fftn_cols(L)), (unsigned)k);
+            if (inv) fftn_launch(k_fftn_crop_z<L, true>, g, fftn_smem<L>(), st, true,
                                  (const float2*)Av, G, dec[0], dec[1], dec[2], N1, N2,
                                  nrows, fftn_tw(*f, 2), fv, K);
-            else fftn_launch(k_fftn_crop_z<L, false>, g, fft_smem<L>(), st, true,
+            else fftn_launch(k_fftn_crop_z<L, false>, g, fftn_smem<L>(), st, true,
                              (const float2*)Av, G, dec[0], dec[1], dec[2], N1, N2, nrows,
                              fftn_tw(*f, 2), fv, K);
         });

@@ -39,6 +39,10 @@ constexpr int kSpinLimit = 1 << 22;
 #ifndef NUFFT_TMA_MINB
 #define NUFFT_TMA_MINB 3
 #endif
+// Threads per CTA of the 3-D TMA-staged interpolation.
+#ifndef NUFFT_TMA_THREADS
+#define NUFFT_TMA_THREADS 256
+#endif
 
 __host__ __device__ __forceinline__ int tma_buffer_cells(const TileGeom& tg, int B2) {
     return ((tg.T[0] * tg.T[1] * B2) + 15) & ~15;
@@ -177,7 +181,7 @@ __device__ __forceinline__ float2 gather3(const float2* tv, int S, int PS,
 }
 
 template <int W>
-__global__ void __launch_bounds__(256, NUFFT_TMA_MINB)
+__global__ void __launch_bounds__(NUFFT_TMA_THREADS, NUFFT_TMA_MINB)
 k_interp_tma(const __grid_constant__ CUtensorMap tmap, const float2* __restrict__ grid,
              int v0, int nvg, int B2, const uint32_t* __restrict__ perm,
              CellPtrs cells, const float2* __restrict__ phase,
@@ -586,8 +590,9 @@ void interp_tma_impl(const PointSet& ps, const TileGeom& tg, const CUtensorMap& 
         const int nv = std::min(nvg, nvec - v0);
         const size_t smem = 2 * nv * per;
         ensure_smem((const void*)k, smem);
-        const int blocks = persistent_grid((const void*)k, smem, ps.nsub);
-        k<<<blocks, 256, smem, st>>>(map, grid, v0, nv, B2,
+        const int blocks = persistent_grid((const void*)k, smem, ps.nsub,
+                                           NUFFT_TMA_THREADS);
+        k<<<blocks, NUFFT_TMA_THREADS, smem, st>>>(map, grid, v0, nv, B2,
                                      ps.sorted ? ps.perm : nullptr, cell_ptrs(ps),
                                      ps.phase, ps.subs, (int)ps.nsub, ps.sched,
                                      out + v0 * ostride, ostride, tg, err);

@@ -200,6 +200,82 @@ __global__ void k_sub_fill(const uint32_t* count, const uint32_t* start,
     }
 }
 
+// Block-wide exclusive scan of a[0..n) in place (a CTA of 256 threads, each
+// owning a contiguous run); returns the total.  warp_tot: 8 words.
+__device__ uint32_t block_exclusive_scan(uint32_t* a, int n, uint32_t* warp_tot) {
+    const int per = (n + blockDim.x - 1) / blockDim.x;
+    const int b = threadIdx.x * per, e = min(n, b + per);
+    uint32_t run = 0;
+    for (int q = b; q < e; ++q) run += a[q];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    uint32_t incl = run;
+#pragma unroll
+    for (int k = 1; k < 32; k <<= 1) {
+        const uint32_t v = __shfl_up_sync(0xffffffffu, incl, k);
+        if (lane >= k) incl += v;
+    }
+    if (lane == 31) warp_tot[wid] = incl;
+    __syncthreads();
+    uint32_t before = incl - run, total = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+        if (w < wid) before += warp_tot[w];
+        total += warp_tot[w];
+    }
+    for (int q = b; q < e; ++q) {
+        const uint32_t v = a[q];
+        a[q] = before;
+        before += v;
+    }
+    __syncthreads();
+    return total;
+}
+
+// Ranks inside residue classes: entries e = 0..n-1 hold a residue key[e] in
+// 0..15; afterwards key[e] = r | k << 4 with k the number of earlier
+// entries of residue r, and rcount[r] the entries of residue r.  A ballot
+// multi-split over 256 entries at a time.
+__device__ void residue_ranks(uint32_t* key, int n, uint32_t* rcount,
+                              uint32_t (*wres)[16]) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    if (threadIdx.x < 16) rcount[threadIdx.x] = 0u;
+    for (int base = 0; base < n; base += blockDim.x) {
+        if (threadIdx.x < 128) wres[threadIdx.x >> 4][threadIdx.x & 15] = 0u;
+        __syncthreads();
+        const int pe = base + threadIdx.x;
+        const bool act = pe < n;
+        const uint32_t r = act ? key[pe] : 16u;           // 16: no residue
+        const unsigned mask = __match_any_sync(0xffffffffu, r);
+        const uint32_t below = (uint32_t)__popc(mask & ((1u << lane) - 1u));
+        if (act && below == 0) wres[wid][r] = (uint32_t)__popc(mask);
+        __syncthreads();
+        if (act) {
+            uint32_t k = rcount[r] + below;
+            for (int w = 0; w < wid; ++w) k += wres[w][r];
+            key[pe] = r | (k << 4);
+        }
+        __syncthreads();
+        if (threadIdx.x < 16) {
+            uint32_t s = 0;
+            for (int w = 0; w < 8; ++w) s += wres[w][threadIdx.x];
+            rcount[threadIdx.x] += s;
+        }
+        __syncthreads();
+    }
+}
+
+// Rank of (k, r) in lexicographic order among the entries counted in
+// rcount: sum_{r'} min(n_{r'}, k) + #{r' < r : n_{r'} > k}.
+__device__ __forceinline__ uint32_t lex_rank(uint32_t kr, const uint32_t* rcount) {
+    const uint32_t r = kr & 15u, k = kr >> 4;
+    uint32_t pos = 0;
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+        const uint32_t n = rcount[q];
+        pos += min(n, k) + ((uint32_t)q < r && n > k ? 1u : 0u);
+    }
+    return pos;
+}
+
 // Order the points of every subproblem by their cell inside the bin
 // (row-major, last dimension fastest, the tile's memory order), and -- when
 // cp.rs is set -- deal them round-robin over the 16 bank residues of their
@@ -209,16 +285,13 @@ __global__ void k_sub_fill(const uint32_t* count, const uint32_t* start,
 //     block-wide exclusive scan give each point its cell-order position c;
 //  2. (interleave) residue r = (sum_d l_d rs[d]) mod 16 of the point's
 //     tile index; k = rank of the point among the residue-r points in cell
-//     order (a ballot multi-split over the cell-ordered residues);
-//  3. the output position is the rank of (k, r) in lexicographic order:
-//     sum_{r'} min(n_{r'}, k) + #{r' < r : n_{r'} > k}, n_r the residue
-//     counts -- so every run of 16 consecutive points (a half-warp of the
+//     order (a ballot multi-split);
+//  3. the output position is the rank of (k, r) in lexicographic order,
+//     so every run of 16 consecutive points (a half-warp of the
 //     interpolation kernels, one point per lane) holds 16 distinct residues
 //     wherever the buckets allow, and the lanes' 8-byte tap loads hit 16
-//     distinct bank pairs;
-// then scatter of cells and permutation into the output arrays (same
-// segment of the sorted order).  Shared memory: (cells per bin + msub
-// [+ msub with the interleave]) x 4 bytes.
+//     distinct bank pairs.
+// Shared memory: (cells per bin + 2 msub) x 4 bytes.
 template <int DIM>
 __global__ void __launch_bounds__(256)
 k_sub_sort(const int4* __restrict__ subs, CellParams cp, int mcells, int msub,
@@ -229,7 +302,7 @@ k_sub_sort(const int4* __restrict__ subs, CellParams cp, int mcells, int msub,
     extern __shared__ uint32_t sm[];
     uint32_t* hist = sm;              // mcells counters, then starts
     uint32_t* slot = sm + mcells;     // per point: local cell | rank << 16
-    uint32_t* kres = slot + msub;     // per cell-order position: r | k << 4
+    uint32_t* kres = slot + msub;     // per cell-order position: residue, then r | k << 4
     __shared__ uint32_t warp_tot[8];
     __shared__ uint32_t rcount[16];
     __shared__ uint32_t wres[8][16];
@@ -246,8 +319,17 @@ k_sub_sort(const int4* __restrict__ subs, CellParams cp, int mcells, int msub,
         }
     }
     const int2* in[3] = {i0, i1, i2};
+    auto residue = [&](int t) {
+        int tix = 0;
+#pragma unroll
+        for (int d = 0; d < DIM; ++d) {
+            int l = in[d][start + t].x - o[d];
+            l = min(max(l, 0), cp.m[d] - 1);
+            tix += l * cp.rs[d];
+        }
+        return (uint32_t)tix & 15u;
+    };
     for (int q = threadIdx.x; q < mcells; q += blockDim.x) hist[q] = 0u;
-    if (threadIdx.x < 16) rcount[threadIdx.x] = 0u;
     __syncthreads();
     for (int t = threadIdx.x; t < cnt; t += blockDim.x) {
         uint32_t loc = 0;
@@ -261,94 +343,31 @@ k_sub_sort(const int4* __restrict__ subs, CellParams cp, int mcells, int msub,
         slot[t] = loc | (r << 16);
     }
     __syncthreads();
-    // exclusive scan of hist: each thread owns a contiguous run
-    const int per = (mcells + blockDim.x - 1) / blockDim.x;
-    const int b = threadIdx.x * per, e = min(mcells, b + per);
-    uint32_t run = 0;
-    for (int q = b; q < e; ++q) run += hist[q];
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    uint32_t incl = run;
-#pragma unroll
-    for (int k = 1; k < 32; k <<= 1) {
-        const uint32_t v = __shfl_up_sync(0xffffffffu, incl, k);
-        if (lane >= k) incl += v;
-    }
-    if (lane == 31) warp_tot[wid] = incl;
-    __syncthreads();
-    uint32_t before = incl - run;
-    for (int w = 0; w < wid; ++w) before += warp_tot[w];
-    for (int q = b; q < e; ++q) {
-        const uint32_t v = hist[q];
-        hist[q] = before;
-        before += v;
-    }
-    __syncthreads();
+    block_exclusive_scan(hist, mcells, warp_tot);
     int2* out[3] = {o0, o1, o2};
+    auto put = [&](int t, int pos) {
+#pragma unroll
+        for (int d = 0; d < DIM; ++d) out[d][start + pos] = in[d][start + t];
+        pout[start + pos] = pin[start + t];
+    };
     if (!inter) {
         for (int t = threadIdx.x; t < cnt; t += blockDim.x) {
             const uint32_t sl = slot[t];
-            const int pos = start + (int)(hist[sl & 0xffffu] + (sl >> 16));
-#pragma unroll
-            for (int d = 0; d < DIM; ++d) out[d][pos] = in[d][start + t];
-            pout[pos] = pin[start + t];
+            put(t, (int)(hist[sl & 0xffffu] + (sl >> 16)));
         }
         return;
     }
-    // 2. cell-order position c of every point and its residue at c
+    // cell-order position c of every point and its residue
     for (int t = threadIdx.x; t < cnt; t += blockDim.x) {
         const uint32_t sl = slot[t];
         const uint32_t c = hist[sl & 0xffffu] + (sl >> 16);
-        int tix = 0;
-#pragma unroll
-        for (int d = 0; d < DIM; ++d) {
-            int l = in[d][start + t].x - o[d];
-            l = min(max(l, 0), cp.m[d] - 1);
-            tix += l * cp.rs[d];
-        }
-        kres[c] = (uint32_t)tix & 15u;
+        kres[c] = residue(t);
         slot[t] = c;
     }
     __syncthreads();
-    //    rank k among the same-residue points, in cell order, 256 at a time
-    for (int base = 0; base < cnt; base += blockDim.x) {
-        if (threadIdx.x < 128) wres[threadIdx.x >> 4][threadIdx.x & 15] = 0u;
-        __syncthreads();
-        const int pe = base + threadIdx.x;
-        const bool act = pe < cnt;
-        const uint32_t r = act ? kres[pe] : 16u;          // 16: no residue
-        const unsigned mask = __match_any_sync(0xffffffffu, r);
-        const uint32_t below = (uint32_t)__popc(mask & ((1u << lane) - 1u));
-        if (act && below == 0) wres[wid][r] = (uint32_t)__popc(mask);
-        __syncthreads();
-        if (act) {
-            uint32_t k = rcount[r] + below;
-            for (int w = 0; w < wid; ++w) k += wres[w][r];
-            kres[pe] = r | (k << 4);
-        }
-        __syncthreads();
-        if (threadIdx.x < 16) {
-            uint32_t s = 0;
-#pragma unroll
-            for (int w = 0; w < 8; ++w) s += wres[w][threadIdx.x];
-            rcount[threadIdx.x] += s;
-        }
-        __syncthreads();
-    }
-    // 3. position = rank of (k, r) in lexicographic order
-    for (int t = threadIdx.x; t < cnt; t += blockDim.x) {
-        const uint32_t kr = kres[slot[t]];
-        const uint32_t r = kr & 15u, k = kr >> 4;
-        uint32_t pos = 0;
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-            const uint32_t n = rcount[q];
-            pos += min(n, k) + ((uint32_t)q < r && n > k ? 1u : 0u);
-        }
-        const int g = start + (int)pos;
-#pragma unroll
-        for (int d = 0; d < DIM; ++d) out[d][g] = in[d][start + t];
-        pout[g] = pin[start + t];
-    }
+    residue_ranks(kres, cnt, rcount, wres);
+    for (int t = threadIdx.x; t < cnt; t += blockDim.x)
+        put(t, (int)lex_rank(kres[slot[t]], rcount));
 }
 
 // Type-3 phases, written in sorted order (position j reads caller index

@@ -219,3 +219,26 @@ def test_type2_3d_batch_tma_staged_tiles(N, rng):
         np.testing.assert_array_equal(got[b], one)
         exact = fast.direct_t2([v[idx] for v in x], fks[b], -1)
         assert port.rel_l2(got[b][idx], exact) <= 1e-5
+
+
+@pytest.mark.parametrize("isign", [-1, +1])
+def test_type2_3d_dense_point_pairs(isign, rng):
+    """Dense 3-D interpolation subproblems (thousands of points per 10^3
+    bin, many points per cell): the sort pairs points of one cell and the
+    TMA-staged kernel gathers each pair in one pass over the taps (odd
+    cells leave single points, gathered two per thread, the last one
+    alone).  Every output against the fp64 restatement of the pipeline,
+    and a sample against the exact sum."""
+    from mlx_nufft_b200 import Type2PlanND
+    N, M = (24, 20, 28), 300_001
+    x = [np.mod(rng.normal(0, 0.25, M) + np.pi, 2 * np.pi) - np.pi for _ in range(3)]
+    x[0][:1000] = rng.uniform(-np.pi, np.pi, 1000)       # a sparse fringe too
+    fk = rng.standard_normal(N) + 1j * rng.standard_normal(N)
+    plan = Type2PlanND(tuple(x), N, eps=1e-6, isign=isign)
+    assert plan._plan.info().tiled
+    c = plan.execute(fk)
+    assert port.rel_l2(c, port.nufft_t2(x, fk, 1e-6, isign)) <= 2e-5
+    idx = rng.choice(M, 200, replace=False)
+    assert port.rel_l2(c[idx], fast.direct_t2(x, fk, isign, idx)) <= gate(1e-6)
+    # deterministic: a second execute is bit-identical
+    np.testing.assert_array_equal(plan.execute(fk), c)
