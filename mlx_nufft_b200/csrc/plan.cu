@@ -266,7 +266,8 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
     // 1536: 0.092, 2048: 0.105 -- its stages leave 3 CTAs per SM, not 4)
     const int m1 = m1d > 0 ? m1d : (interp ? 1792 : 1024);
     static const int m3i = env_int("NUFFT_BIN_3D_INTERP", 0);
-    const int m3 = interp ? (m3i > 0 ? m3i : 10) : 8;
+    static const int m3s = env_int("NUFFT_BIN_3D_SPREAD", 0);   // tuning
+    const int m3 = interp ? (m3i > 0 ? m3i : 10) : (m3s > 0 ? m3s : 8);
     static const int m2d = env_int("NUFFT_BIN_2D", 0);
     const int m2 = m2d > 0 ? m2d : 32;
     int m0 = dim == 1 ? m1 : (dim == 2 ? m2 : m3);
