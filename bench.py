@@ -892,7 +892,7 @@ def run_split(ctx, gen, k, steps, warmup, headline, scale):
         units = int(cfg["x"][0].size)
         stage_ms = stage_split(ctx, native, step, max(1, min(steps, 10)))
         # variant: rank 0 builds the grid, NCCL broadcast, every rank interps
-        grid = par.plan_grid_view(native, [int(info.n_up[d]) for d in range(int(info.dim))])
+        grid = par.plan_grid_storage(native)          # stored layout, halo included
         gview = torch.view_as_real(grid)
         from mlx_nufft_b200 import _lib
 

@@ -104,6 +104,12 @@ typedef struct nufft_plan_info {
     int     fft_own;               /* 1 if this library's own FFT (two-pass 1-D,
                                       or pruned three-pass 3-D; pad / crop fused)
                                       replaces pad + cuFFT (+ crop)                  */
+    int64_t grid_cells;            /* cells per stored fine grid: the n_up product,
+                                      plus a periodic halo for 3-D type 2 on the
+                                      pruned FFT (nufft_get_grid's layout)           */
+    int64_t grid_ext[3];           /* stored extents per dimension (n_up + halo)    */
+    int     grid_lo[3];            /* index of fine-grid cell 0 per dimension in the
+                                      stored extents (halo cells below it)          */
 } nufft_plan_info;
 
 /* Fill `opts` with the defaults above. */
@@ -179,10 +185,12 @@ int nufft_execute_adjoint(nufft_plan_t plan, const void* in, void* out,
 int nufft_execute_stage(nufft_plan_t plan, int stage, const void* in,
                         void* out, int nvec, void* stream);
 
-/* Device address and size (elements, all n_trans grids) of the plan's fine
- * grid, e.g. for a collective between the stages above: type 1 the
- * complex64 spreading grid; type 2 the FFT grid, complex128 when the plan
- * runs its FFT in fp64 (nufft_plan_info.fft64), else complex64.            */
+/* Device address and size (elements, all grids the plan holds) of the
+ * plan's fine grid, e.g. for a collective between the stages above: type 1
+ * the complex64 spreading grid; type 2 the FFT grid, complex128 when the
+ * plan runs its FFT in fp64 (nufft_plan_info.fft64), else complex64.  Grids
+ * are grid_cells apart in the stored layout of nufft_plan_info (grid_ext,
+ * grid_lo: a periodic halo around a 3-D type-2 grid on the pruned FFT).    */
 int nufft_get_grid(nufft_plan_t plan, void** grid, int64_t* n_complex);
 
 /* Type 1 only: transform G disjoint subsets of the plan's points

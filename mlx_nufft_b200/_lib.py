@@ -71,6 +71,9 @@ class NufftPlanInfo(ctypes.Structure):
         ("fft_execs", ctypes.c_int64),
         ("fft64", ctypes.c_int),
         ("fft_own", ctypes.c_int),
+        ("grid_cells", ctypes.c_int64),
+        ("grid_ext", ctypes.c_int64 * 3),
+        ("grid_lo", ctypes.c_int * 3),
     ]
 
 

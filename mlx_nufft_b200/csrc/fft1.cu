@@ -495,32 +495,38 @@ k_fftn_pad_z(const float2* __restrict__ f, int64_t f_vs, const float* __restrict
              float2* __restrict__ A, int64_t A_vs) {
     constexpr int C = fftn_cols(L);
     extern __shared__ float2 s[];
+    __shared__ float s_d01[C];                   // row corrections d0 * d1
     const int r0 = blockIdx.x * C;
     const int rows = min(C, nrows - r0);
     f += blockIdx.y * f_vs + (int64_t)r0 * N2;
     A += blockIdx.y * A_vs + (int64_t)r0 * L;
-    // K loads in flight per thread before their shared stores
+    if (threadIdx.x < rows) {
+        const int r = r0 + threadIdx.x;
+        s_d01[threadIdx.x] = __ldg(d0 + r / N1) * __ldg(d1 + r % N1);
+    }
+    __syncthreads();
+    // thread t loads mode m = t (+ multiples of the block) of every row, K
+    // rows in flight before their shared stores; mode m = k + N2/2 sits at
+    // fine cell k mod L
     constexpr int K = 8;
-    for (int q0 = threadIdx.x; q0 < C * N2; q0 += K * kFftThreads) {
-        float2 x[K];
-        int dst[K];
+    for (int m = threadIdx.x; m < N2; m += kFftThreads) {
+        const float dm = __ldg(d2 + m);
+        const int cell = ((m - N2 / 2 + L) % L) * C;
+        for (int c0 = 0; c0 < C; c0 += K) {
+            float2 x[K];
 #pragma unroll
-        for (int k = 0; k < K; ++k) {
-            const int q = q0 + k * kFftThreads;
-            const int c = q / N2, m = q - c * N2;
-            // mode m = k + N2/2 sits at fine cell k mod L
-            dst[k] = q < C * N2 ? fpad(((m - N2 / 2 + L) % L) * C + c) : -1;
-            x[k] = make_float2(0.0f, 0.0f);
-            if (q < C * N2 && c < rows) {
-                const int r = r0 + c;
-                const float d = __ldg(d0 + r / N1) * __ldg(d1 + r % N1) * __ldg(d2 + m);
-                const float2 g = __ldg(f + q);
-                x[k] = make_float2(g.x * d, g.y * d);
+            for (int k = 0; k < K; ++k) {
+                const int c = c0 + k;
+                x[k] = make_float2(0.0f, 0.0f);
+                if (c < rows) {
+                    const float d = s_d01[c] * dm;
+                    const float2 g = __ldg(f + (int64_t)c * N2 + m);
+                    x[k] = make_float2(g.x * d, g.y * d);
+                }
             }
-        }
 #pragma unroll
-        for (int k = 0; k < K; ++k)
-            if (dst[k] >= 0) s[dst[k]] = x[k];
+            for (int k = 0; k < K; ++k) s[fpad(cell + c0 + k)] = x[k];
+        }
     }
     for (int q = threadIdx.x; q < C * (L - N2); q += kFftThreads) {
         const int c = q % C, i = N2 - N2 / 2 + q / C;     // out-of-band fine cells
@@ -561,11 +567,14 @@ k_fftn_pad_y(const float2* __restrict__ A, int64_t A_vs, int N1, int n2,
     fft_stages_c<L, 1, INV, C>(s, twL, load, store);
 }
 
-// pass X of the pad: columns (y, z0 + c); blockIdx.y = y
-template <int L, bool INV>
+// pass X of the pad: columns (y, z0 + c); blockIdx.y = y.  HALO: the grid
+// is stored with the periodic halo h (GridHalo); this pass writes the
+// interior, k_halo_fill the halo copies.
+template <int L, bool INV, bool HALO, bool PRUNE>
 __global__ void __launch_bounds__(kFftThreads, NUFFT_FFTN_MINB)
 k_fftn_pad_x(const float2* __restrict__ B, int64_t B_vs, int N0, int n1, int n2,
-             const float2* __restrict__ twL, float2* __restrict__ G, int64_t G_vs) {
+             const float2* __restrict__ twL, float2* __restrict__ G, int64_t G_vs,
+             GridHalo h, const uint8_t* __restrict__ need) {
     constexpr int C = fftn_cols(L);
     extern __shared__ float2 s[];
     grid_dep_sync();
@@ -579,11 +588,73 @@ k_fftn_pad_x(const float2* __restrict__ B, int64_t B_vs, int N0, int n1, int n2,
                       : make_float2(0.0f, 0.0f);
     };
     auto store = [&](int c, int base, int stride, auto& vals) {
+        if constexpr (!HALO) {
 #pragma unroll
-        for (int k = 0; k < vals_len<decltype(vals)>(); ++k)
-            G[((int64_t)(base + k * stride) * n1 + y) * n2 + z0 + c] = vals[k];
+            for (int k = 0; k < vals_len<decltype(vals)>(); ++k)
+                G[((int64_t)(base + k * stride) * n1 + y) * n2 + z0 + c] = vals[k];
+        } else {
+            const int64_t PP = (int64_t)h.P[1] * h.P[2];
+            const int64_t yz = (y + h.lo[1]) * h.P[2] + h.lo[2] + z0 + c;
+#pragma unroll
+            for (int k = 0; k < vals_len<decltype(vals)>(); ++k) {
+                const int xs = base + k * stride + h.lo[0];
+                if (!PRUNE || __ldg(need + xs)) G[(int64_t)xs * PP + yz] = vals[k];
+            }
+        }
     };
     fft_stages_c<L, 1, INV, C>(s, twL, load, store);
+}
+
+// Periodic halo of nv stored grids (GridHalo h) copied from their
+// interior, one dimension per launch: pass 2 (contiguous dimension) over the
+// interior rows, pass 1 whole rows (their pass-2 halo included) over the
+// interior planes, pass 0 whole planes.  Each halo cell at stored index i'
+// takes the cell one period away (i' + n below the grid, i' - n above it),
+// which lies in the interior since lo, hi <= n.  need (optional): only the
+// stored planes of dimension 0 with need[s] != 0 (whose interior
+// counterparts are marked too).
+__global__ void __launch_bounds__(256)
+k_halo_fill(float2* __restrict__ G, int64_t G_vs, GridHalo h, int n0, int n1, int n2,
+            int pass, const uint8_t* __restrict__ need) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    G += blockIdx.y * G_vs;
+    const int64_t P2 = h.P[2], PP = (int64_t)h.P[1] * h.P[2];
+    auto src = [](int k, int lo, int n, int& dst) {
+        dst = k < lo ? k : n + k;            // k: index among the halo cells
+        return k < lo ? dst + n : dst - n;
+    };
+    if (pass == 2) {
+        const int hz = h.lo[2] + h.hi[2];
+        if (i >= (int64_t)n0 * n1 * hz) return;
+        const int64_t r = i / hz;
+        const int k = (int)(i - r * hz);
+        const int x = (int)(r / n1), y = (int)(r - (int64_t)x * n1);
+        if (need && !need[x + h.lo[0]]) return;
+        int zd;
+        const int zs = src(k, h.lo[2], n2, zd);
+        float2* row = G + (int64_t)(x + h.lo[0]) * PP + (int64_t)(y + h.lo[1]) * P2;
+        row[zd] = row[zs];
+    } else if (pass == 1) {
+        const int hy = h.lo[1] + h.hi[1];
+        if (i >= (int64_t)n0 * hy * P2) return;
+        const int64_t r = i / P2;
+        const int64_t z = i - r * P2;
+        const int x = (int)(r / hy), k = (int)(r - (int64_t)x * hy);
+        if (need && !need[x + h.lo[0]]) return;
+        int yd;
+        const int ys = src(k, h.lo[1], n1, yd);
+        float2* pl = G + (int64_t)(x + h.lo[0]) * PP;
+        pl[yd * P2 + z] = pl[ys * P2 + z];
+    } else {
+        const int hx = h.lo[0] + h.hi[0];
+        if (i >= (int64_t)hx * PP) return;
+        const int k = (int)(i / PP);
+        const int64_t q = i - (int64_t)k * PP;
+        int xd;
+        const int xs = src(k, h.lo[0], n0, xd);
+        if (need && !need[xd]) return;
+        G[xd * PP + q] = G[xs * PP + q];
+    }
 }
 
 // pass X of the crop: columns (y, z0 + c) of the full grid, in-band x only
@@ -647,6 +718,7 @@ k_fftn_crop_z(const float2* __restrict__ A, int64_t A_vs, const float* __restric
               float2* __restrict__ f, int64_t f_vs) {
     constexpr int C = fftn_cols(L);
     extern __shared__ float2 s[];
+    __shared__ float s_d01[C];                   // row corrections d0 * d1
     grid_dep_sync();
     const int r0 = blockIdx.x * C;
     const int rows = min(C, nrows - r0);
@@ -669,14 +741,21 @@ k_fftn_crop_z(const float2* __restrict__ A, int64_t A_vs, const float* __restric
     __syncthreads();
     auto none = [](int, int) { return make_float2(0.0f, 0.0f); };
     auto nost = [](int, int, int, auto&) {};
+    if (threadIdx.x < rows) {
+        const int r = r0 + threadIdx.x;
+        s_d01[threadIdx.x] = __ldg(d0 + r / N1) * __ldg(d1 + r % N1);
+    }
     fft_stages_c<L, 1, INV, C, true>(s, twL, none, nost);
     __syncthreads();
-    for (int q = threadIdx.x; q < rows * N2; q += kFftThreads) {
-        const int c = q / N2, m = q - c * N2;
-        const int r = r0 + c;
-        const float d = __ldg(d0 + r / N1) * __ldg(d1 + r % N1) * __ldg(d2 + m);
-        const float2 x = s[fpad(((m - N2 / 2 + L) % L) * C + c)];
-        f[q] = make_float2(x.x * d, x.y * d);
+    // thread t stores mode m = t (+ multiples of the block) of every row
+    for (int m = threadIdx.x; m < N2; m += kFftThreads) {
+        const float dm = __ldg(d2 + m);
+        const int cell = ((m - N2 / 2 + L) % L) * C;
+        for (int c = 0; c < rows; ++c) {
+            const float d = s_d01[c] * dm;
+            const float2 x = s[fpad(cell + c)];
+            f[(int64_t)c * N2 + m] = make_float2(x.x * d, x.y * d);
+        }
     }
 }
 
@@ -755,11 +834,18 @@ void fftn_reserve(Fftn* f, int nv) {
 }
 
 void fftn_pad(Fftn* f, const float2* modes, const float* const* dec, float2* grid,
-              int nv, bool inv, cudaStream_t st) {
+              int nv, bool inv, cudaStream_t st, const GridHalo* halo,
+              const uint8_t* need) {
+    if (!halo) need = nullptr;
     fftn_reserve(f, nv);
     const int n0 = f->n[0], n1 = f->n[1], n2 = f->n[2];
     const int N0 = f->N[0], N1 = f->N[1], N2 = f->N[2];
-    const int64_t K = (int64_t)N0 * N1 * N2, G = (int64_t)n0 * n1 * n2;
+    // cells per stored grid (with the halo, if any); the first pass's
+    // output A also lives in each grid's memory
+    const int64_t K = (int64_t)N0 * N1 * N2,
+                  G = halo ? (int64_t)halo->P[0] * halo->P[1] * halo->P[2]
+                           : (int64_t)n0 * n1 * n2;
+    const GridHalo h = halo ? *halo : GridHalo{};
     const int64_t Bs = fftn_scratch_cells(*f);
     float2* A = grid;            // A[m0][m1][z] in the grid's own memory
     float2* B = f->tmp;
@@ -788,12 +874,39 @@ void fftn_pad(Fftn* f, const float2* modes, const float* const* dec, float2* gri
         NUFFT_LAUNCH("k_fftn_pad_y");
         NUFFT_FFT_LEN_SWITCH(n0, {
             dim3 g((unsigned)(n2 / fftn_cols(L)), (unsigned)n1, (unsigned)k);
-            if (inv) fftn_launch(k_fftn_pad_x<L, true>, g, fftn_smem<L>(), st, true,
-                                 (const float2*)Bv, Bs, N0, n1, n2, fftn_tw(*f, 0), Gv, G);
-            else fftn_launch(k_fftn_pad_x<L, false>, g, fftn_smem<L>(), st, true,
-                             (const float2*)Bv, Bs, N0, n1, n2, fftn_tw(*f, 0), Gv, G);
+            const float2* Bc = Bv;
+            const float2* tw = fftn_tw(*f, 0);
+            const size_t sm = fftn_smem<L>();
+            if (need) {
+                if (inv) fftn_launch(k_fftn_pad_x<L, true, true, true>, g, sm, st, true,
+                                     Bc, Bs, N0, n1, n2, tw, Gv, G, h, need);
+                else fftn_launch(k_fftn_pad_x<L, false, true, true>, g, sm, st, true,
+                                 Bc, Bs, N0, n1, n2, tw, Gv, G, h, need);
+            } else if (halo) {
+                if (inv) fftn_launch(k_fftn_pad_x<L, true, true, false>, g, sm, st, true,
+                                     Bc, Bs, N0, n1, n2, tw, Gv, G, h, need);
+                else fftn_launch(k_fftn_pad_x<L, false, true, false>, g, sm, st, true,
+                                 Bc, Bs, N0, n1, n2, tw, Gv, G, h, need);
+            } else {
+                if (inv) fftn_launch(k_fftn_pad_x<L, true, false, false>, g, sm, st, true,
+                                     Bc, Bs, N0, n1, n2, tw, Gv, G, h, need);
+                else fftn_launch(k_fftn_pad_x<L, false, false, false>, g, sm, st, true,
+                                 Bc, Bs, N0, n1, n2, tw, Gv, G, h, need);
+            }
         });
         NUFFT_LAUNCH("k_fftn_pad_x");
+        if (halo) {
+            const int64_t work[3] = {
+                (int64_t)(h.lo[0] + h.hi[0]) * h.P[1] * h.P[2],
+                (int64_t)n0 * (h.lo[1] + h.hi[1]) * h.P[2],
+                (int64_t)n0 * n1 * (h.lo[2] + h.hi[2])};
+            for (int pass = 2; pass >= 0; --pass) {
+                if (work[pass] == 0) continue;
+                const dim3 g((unsigned)((work[pass] + 255) / 256), (unsigned)k);
+                k_halo_fill<<<g, 256, 0, st>>>(Gv, G, h, n0, n1, n2, pass, need);
+                NUFFT_LAUNCH("k_halo_fill");
+            }
+        }
     }
 }
 

@@ -122,6 +122,37 @@ struct TileGeom {
     // 8-byte bank pairs; rounds = ceil(W^2 / 32).
     int S2;
     uint8_t tapmap[kMaxTapRounds * 32];
+    // the same for tiles of vector pairs (16-byte cells, one float4 = two
+    // vectors' complex64): row stride S4, each quarter-warp's 8 accesses
+    // on 8 distinct 16-byte bank quads
+    int S4;
+    uint8_t tapmap4[kMaxTapRounds * 32];
+    // Layout of the grid a 3-D interpolation reads (GridHalo): cell i of
+    // dimension d at index i + lo[d] of an extent P[d] = lo[d] + n[d] + hi,
+    // pcells cells per vector.  No halo: lo = 0, P = n, pcells = ncells.
+    int lo[3];
+    int P[3];
+    int64_t pcells;
+};
+
+// The no-halo layout (lo = 0, P = n, pcells = ncells) of a geometry whose
+// n and ncells are set.
+inline void set_no_halo(TileGeom& tg) {
+    for (int d = 0; d < 3; ++d) {
+        tg.lo[d] = 0;
+        tg.P[d] = tg.n[d];
+    }
+    tg.pcells = tg.ncells;
+}
+
+// Periodic halo of a 3-D fine grid: the cells within lo[d] below and hi[d]
+// above the grid in dimension d hold copies of the cells one period away,
+// so that every tile of a 3-D interpolation lies inside the stored array
+// (no wrap).  P[d] = lo[d] + n[d] + hi[d].
+struct GridHalo {
+    int lo[3];
+    int hi[3];
+    int P[3];
 };
 
 // Elements allocated past M in every per-point array (cells, permutation,
@@ -218,9 +249,13 @@ bool fftn_supported(const int64_t* n);
 void fftn_init(Fftn* f, const int64_t* n, const int64_t* N);
 void fftn_free(Fftn* f);
 int64_t fftn_scratch_cells(const Fftn& f);
-// nv mode boxes (times the corrections dec[d]) -> nv transformed fine grids
+// nv mode boxes (times the corrections dec[d]) -> nv transformed fine grids;
+// with a halo (non-null) each grid is stored padded, halo copies included,
+// prod P cells apart; with need (halo only) just the stored planes of
+// dimension 0 with need[s] != 0 are written
 void fftn_pad(Fftn* f, const float2* modes, const float* const* dec, float2* grid,
-              int nv, bool inv, cudaStream_t st);
+              int nv, bool inv, cudaStream_t st, const GridHalo* halo = nullptr,
+              const uint8_t* need = nullptr);
 // nv fine grids -> nv mode boxes of the transform times dec[d]; the grids are
 // overwritten (used as scratch)
 void fftn_crop(Fftn* f, float2* grid, const float* const* dec, float2* modes, int nv,
@@ -280,6 +315,11 @@ bool make_grid_tmap(CUtensorMap* map, const float2* grid, const TileGeom& tg,
                     int nbatch);
 // Row stride (cells) of the TMA-staged 3-D tile: T[2] + 1 rounded up to even.
 int tma_box_x(const TileGeom& tg);
+// need[s] = 1 for every stored plane s (dimension 0, halo layout of tg) that
+// a tile of the point set's subproblems covers, and for the interior plane
+// each of those copies (one period away); need[] is not cleared first.
+void mark_tile_planes(const PointSet& ps, const TileGeom& tg, uint8_t* need,
+                      cudaStream_t st);
 bool launch_interp_tma(const PointSet& ps, const TileGeom& tg, int w,
                        const CUtensorMap* map, const float2* grid, int nvec,
                        float2* out, int64_t ostride, int* err, cudaStream_t st);

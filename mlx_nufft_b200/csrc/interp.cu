@@ -24,7 +24,7 @@ void interp_impl(const PointSet& ps, const TileGeom& tg, const G* grid,
             ensure_smem((const void*)k, smem);
             const int blocks = persistent_grid((const void*)k, smem, ps.nsub);
             k<<<blocks, 256, smem, st>>>(
-                grid + v0 * tg.ncells, nv, perm, cells, ps.phase, ps.subs,
+                grid + v0 * tg.pcells, nv, perm, cells, ps.phase, ps.subs,
                 (int)ps.nsub, ps.sched, out + v0 * ostride, ostride, tg);
             NUFFT_LAUNCH("k_interp_tiled");
         }

@@ -14,9 +14,11 @@
 // of 8-byte elements (complex64).  A TMA copy must start at a 16-byte
 // boundary in x, so each tile box starts at the even cell x0 = o_x rounded
 // down and is B2 = T2 + 1 rounded up to even cells wide; the point
-// arithmetic adds the offset o_x - x0 (0 or 1).  Bins whose tile would
-// wrap around the periodic grid (the box is not inside [0, n)) are loaded
-// by the CTA's threads with wrap, into the same padded layout.
+// arithmetic adds the offset o_x - x0 (0 or 1).  A grid stored with a
+// periodic halo (TileGeom lo / P; the pruned 3-D FFT writes one for type 2)
+// holds every tile box; otherwise bins whose tile would wrap around the
+// periodic grid are loaded by the CTA's threads with wrap, into the same
+// padded layout.
 //
 // Every mbarrier wait is bounded: after kSpinLimit polls the CTA records
 // an error in *err (the plan's host-mapped execute error flag, which the
@@ -112,7 +114,7 @@ __device__ __forceinline__ void load_wrapped_tile(float2* tile, const float2* gr
                                                   int tid, int nthr) {
     constexpr int K = 4;
     for (int v = 0; v < nvg; ++v) {
-        const float2* gv = grid + (int64_t)(v0 + v) * tg.ncells;
+        const float2* gv = grid + (int64_t)(v0 + v) * tg.pcells;
         for (int q0 = tid; q0 < tg.tcells; q0 += K * nthr) {
             float2 val[K];
             int sq[K];
@@ -137,7 +139,8 @@ __device__ __forceinline__ void load_wrapped_tile(float2* tile, const float2* gr
 struct TmaBin {
     int o[3];        // tile origin (global cell of tile index 0), per dim
     int x0;          // box start in x (even)
-    bool interior;   // box inside the grid: TMA-loadable
+    int c[3];        // box start in the stored grid (o[0], o[1], x0 + halo lo)
+    bool interior;   // box inside the stored grid: TMA-loadable
 };
 
 __device__ __forceinline__ TmaBin tma_bin(int bin, const TileGeom& tg, int B2,
@@ -145,9 +148,12 @@ __device__ __forceinline__ TmaBin tma_bin(int bin, const TileGeom& tg, int B2,
     TmaBin b;
     bin_origin<3>(bin, tg, b.o);
     b.x0 = b.o[2] - (b.o[2] & 1);
-    b.interior = use_tma && b.o[0] >= 0 && b.o[0] + tg.T[0] <= tg.n[0] &&
-                 b.o[1] >= 0 && b.o[1] + tg.T[1] <= tg.n[1] &&
-                 b.x0 >= 0 && b.x0 + B2 <= tg.n[2];
+    b.c[0] = b.o[0] + tg.lo[0];
+    b.c[1] = b.o[1] + tg.lo[1];
+    b.c[2] = b.x0 + tg.lo[2];
+    b.interior = use_tma && b.c[0] >= 0 && b.c[0] + tg.T[0] <= tg.P[0] &&
+                 b.c[1] >= 0 && b.c[1] + tg.T[1] <= tg.P[1] &&
+                 b.c[2] >= 0 && b.c[2] + B2 <= tg.P[2];
     return b;
 }
 
@@ -213,8 +219,8 @@ k_interp_tma(const __grid_constant__ CUtensorMap tmap, const float2* __restrict_
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mbar_expect_tx(&bar[b], tile_bytes * (uint32_t)nvg);
         for (int v = 0; v < nvg; ++v)
-            tma_load_4d(sbuf + ((size_t)b * nvg + v) * TS, &tmap, bn.x0, bn.o[1],
-                        bn.o[0], v0 + v, &bar[b]);
+            tma_load_4d(sbuf + ((size_t)b * nvg + v) * TS, &tmap, bn.c[2], bn.c[1],
+                        bn.c[0], v0 + v, &bar[b]);
     };
     // ring[b]: subproblem whose tile occupies buffer b.  Thread 0 claims two
     // ahead, so each subproblem needs one CTA barrier (which also releases
@@ -562,12 +568,13 @@ bool make_grid_tmap(CUtensorMap* map, const float2* grid, const TileGeom& tg,
     EncodeTiled enc = encode_tiled();
     if (!enc) return false;
     const int B2 = tma_box_x(tg);
-    if (B2 > 256 || tg.T[1] > 256 || tg.T[0] > 256 || B2 > tg.n[2]) return false;
-    const cuuint64_t dims[4] = {(cuuint64_t)tg.n[2], (cuuint64_t)tg.n[1],
-                                (cuuint64_t)tg.n[0], (cuuint64_t)nbatch};
-    const cuuint64_t strides[3] = {(cuuint64_t)tg.n[2] * 8,
-                                   (cuuint64_t)tg.n[1] * tg.n[2] * 8,
-                                   (cuuint64_t)tg.ncells * 8};
+    if (B2 > 256 || tg.T[1] > 256 || tg.T[0] > 256 || B2 > tg.P[2]) return false;
+    // the stored layout: extents P (n plus the periodic halo, if any)
+    const cuuint64_t dims[4] = {(cuuint64_t)tg.P[2], (cuuint64_t)tg.P[1],
+                                (cuuint64_t)tg.P[0], (cuuint64_t)nbatch};
+    const cuuint64_t strides[3] = {(cuuint64_t)tg.P[2] * 8,
+                                   (cuuint64_t)tg.P[1] * tg.P[2] * 8,
+                                   (cuuint64_t)tg.pcells * 8};
     const cuuint32_t box[4] = {(cuuint32_t)B2, (cuuint32_t)tg.T[1],
                                (cuuint32_t)tg.T[0], 1};
     const cuuint32_t estr[4] = {1, 1, 1, 1};
@@ -577,6 +584,19 @@ bool make_grid_tmap(CUtensorMap* map, const float2* grid, const TileGeom& tg,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
+}
+
+__global__ void k_mark_planes(const int4* __restrict__ subs, int nsub, TileGeom tg,
+                              uint8_t* __restrict__ need) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nsub) return;
+    int o[3];
+    bin_origin<3>(subs[i].z, tg, o);
+    const int n0 = tg.n[0];
+    for (int k = 0; k < tg.T[0]; ++k) {
+        need[o[0] + k + tg.lo[0]] = 1;
+        need[(((o[0] + k) % n0) + n0) % n0 + tg.lo[0]] = 1;
+    }
 }
 
 template <int W>
@@ -618,6 +638,14 @@ void interp1_stream_impl(const PointSet& ps, const TileGeom& tg, const float2* g
                          ostride, tg, err);
         NUFFT_LAUNCH("k_interp1_stream");
     }
+}
+
+void mark_tile_planes(const PointSet& ps, const TileGeom& tg, uint8_t* need,
+                      cudaStream_t st) {
+    if (ps.nsub == 0 || tg.dim != 3) return;
+    const unsigned blocks = (unsigned)((ps.nsub + 255) / 256);
+    k_mark_planes<<<blocks, 256, 0, st>>>(ps.subs, (int)ps.nsub, tg, need);
+    NUFFT_LAUNCH("k_mark_planes");
 }
 
 bool launch_interp_tma(const PointSet& ps, const TileGeom& tg, int w,

@@ -132,6 +132,7 @@ extern "C" int nufft_interp_noalloc(int dim, const int64_t* n_grid, double eps,
                 tg.n[d] = 1;
             }
         }
+        set_no_halo(tg);
         int dev = 0;
         NUFFT_CUDA(cudaGetDevice(&dev));
         int2* cells = (int2*)scratch_address(dev);

@@ -143,6 +143,19 @@ struct nufft_plan_s {
     bool fft64 = false;
     float2* gspread = nullptr;
     float2* gfft = nullptr;
+    // Type 2, 3-D, complex64 with the pruned FFT: gfft is stored with a
+    // periodic halo (gh; tg_src carries the layout), so every tile of the
+    // TMA interpolation lies inside the stored grid.  gcells: cells per
+    // stored FFT grid (nupcells without a halo).
+    bool halo = false;
+    GridHalo gh{};
+    int64_t gcells = 1;
+    // Planes of dimension 0 that the point set's tiles read (halo layout;
+    // device bytes, gh.P[0] of them), set at setpts: an execute's last FFT
+    // pass writes only those when not all are (a plan over one slab of the
+    // points); the stage API's grid is always written whole.
+    uint8_t* xneed = nullptr;
+    bool xneed_all = true;
     std::map<int, cufftHandle> ffts;
     Fft1 fft1;                 // two-pass 1-D FFT (fft1.cu), when in use
     Fftn fftn;                 // pruned 3-D FFT with pad / crop (fft1.cu)
@@ -196,48 +209,57 @@ int interp_msub(int dim) {
 }
 
 // ----------------------------------------------------------------------
-// In-plane tap order of the 3-D plane-owned spread (k_spread_planes): lanes
-// of a half-warp read / write 16 float2 at tile offsets y*S2 + x; they use
-// 16 distinct bank pairs when those offsets are distinct mod 16.  Greedy
-// fill of half-warps with taps of distinct residues, for the smallest row
-// stride S2 >= T2 (up to T2 + 8) that needs only ceil(W^2 / 32) rounds;
-// otherwise the plain order at S2 = T2 (correct, with bank conflicts).
-void plane_tap_order(TileGeom& tg, int w) {
-    std::memset(tg.tapmap, 0xff, sizeof(tg.tapmap));
-    const int T2 = tg.T[2];
+// In-plane tap order of the 3-D plane-owned spread (k_spread_planes).  The
+// lanes of a group of G (16: a half-warp of 8-byte accesses; 8: a
+// quarter-warp of 16-byte ones) read / write one word each at tile offsets
+// y*S + x (in words); the group's accesses are conflict-free when those
+// offsets are distinct mod G.  Greedy fill of groups with taps of distinct
+// residues, for the smallest row stride S >= T2 (up to T2 + 8) that needs
+// only ceil(W^2 / 32) rounds; otherwise the plain order at S = T2
+// (correct, with bank conflicts).  Returns S; map[r * 32 + l] = tap
+// (y << 4 | x) of lane l in round r, 0xff idle.
+int tap_groups(int w, int T2, int G, uint8_t* map, size_t map_bytes) {
+    std::memset(map, 0xff, map_bytes);
     const int rounds = (w * w + 31) / 32;
-    tg.S2 = T2;
-    if (w > kMaxW || rounds > kMaxTapRounds) return;
+    if (w > kMaxW || rounds > kMaxTapRounds) return T2;
     for (int S = T2; S <= T2 + 8; ++S) {
         std::vector<int> left;
         for (int t = 0; t < w * w; ++t) left.push_back(t);
-        std::vector<std::vector<int>> halves;
+        std::vector<std::vector<int>> groups;
         while (!left.empty()) {
-            std::vector<int> half, rest;
+            std::vector<int> grp, rest;
             bool used[16] = {};
             for (int t : left) {
-                const int r = ((t / w) * S + t % w) % 16;
-                if (!used[r] && half.size() < 16) {
+                const int r = ((t / w) * S + t % w) % G;
+                if (!used[r] && (int)grp.size() < G) {
                     used[r] = true;
-                    half.push_back(t);
+                    grp.push_back(t);
                 } else {
                     rest.push_back(t);
                 }
             }
-            halves.push_back(half);
+            groups.push_back(grp);
             left.swap(rest);
         }
-        if ((int)(halves.size() + 1) / 2 > rounds) continue;
-        for (size_t h = 0; h < halves.size(); ++h)
-            for (size_t i = 0; i < halves[h].size(); ++i) {
-                const int t = halves[h][i];
-                tg.tapmap[h * 16 + i] = (uint8_t)(((t / w) << 4) | (t % w));
+        const int per_round = 32 / G;
+        if ((int)(groups.size() + per_round - 1) / per_round > rounds) continue;
+        for (size_t h = 0; h < groups.size(); ++h)
+            for (size_t i = 0; i < groups[h].size(); ++i) {
+                const int t = groups[h][i];
+                map[h * G + i] = (uint8_t)(((t / w) << 4) | (t % w));
             }
-        tg.S2 = S;
-        return;
+        return S;
     }
-    for (int t = 0; t < w * w; ++t)
-        tg.tapmap[t] = (uint8_t)(((t / w) << 4) | (t % w));
+    for (int t = 0; t < w * w; ++t) map[t] = (uint8_t)(((t / w) << 4) | (t % w));
+    return T2;
+}
+
+// Both tap orders of a 3-D spread geometry: 8-byte words (one vector per
+// tile, tapmap / S2) and 16-byte words (two vectors per tile cell,
+// tapmap4 / S4).
+void plane_tap_order(TileGeom& tg, int w) {
+    tg.S2 = tap_groups(w, tg.T[2], 16, tg.tapmap, sizeof(tg.tapmap));
+    tg.S4 = tap_groups(w, tg.T[2], 8, tg.tapmap4, sizeof(tg.tapmap4));
 }
 
 // ----------------------------------------------------------------------
@@ -249,9 +271,15 @@ void plane_tap_order(TileGeom& tg, int w) {
 // 8 x 8 x 8 in 3-D for spreading (room for several vectors' tiles) and
 // 10 x 10 x 10 for 3-D interpolation (more points per subproblem, less halo:
 // measured 21-27 % faster than 8^3 on the 3-D benchmark workloads: 3-D
-// type 2 at 5e7 clustered points and 3-D type 3 at 1e6 -> 1e6).
+// type 2 at 5e7 clustered points and 3-D type 3 at 1e6 -> 1e6).  The
+// TMA-staged complex64 interpolation at w <= 7 takes 12^3 bins (`m3i`):
+// two 18 x 18 x 20-cell buffers per CTA still fit two CTAs per SM, and the
+// larger subproblems even out the bank residues of their points (cfg 4
+// interp 5.37 ms vs 5.67 at 10^3, 5.79 at 11^3, 8.44 at 9^3).
+bool halo_wanted(const nufft_plan_s* p);
+
 TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
-                   bool interp) {
+                   bool interp, int m3i_default = 10) {
     TileGeom tg{};
     tg.dim = dim;
     tg.ncells = 1;
@@ -267,7 +295,7 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
     const int m1 = m1d > 0 ? m1d : (interp ? 1792 : 1024);
     static const int m3i = env_int("NUFFT_BIN_3D_INTERP", 0);
     static const int m3s = env_int("NUFFT_BIN_3D_SPREAD", 0);   // tuning
-    const int m3 = interp ? (m3i > 0 ? m3i : 10) : (m3s > 0 ? m3s : 8);
+    const int m3 = interp ? (m3i > 0 ? m3i : m3i_default) : (m3s > 0 ? m3s : 8);
     static const int m2d = env_int("NUFFT_BIN_2D", 0);
     const int m2 = m2d > 0 ? m2d : 32;
     int m0 = dim == 1 ? m1 : (dim == 2 ? m2 : m3);
@@ -287,9 +315,47 @@ TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
         tg.tdiv[d] = tg.T[d] > 1
             ? (uint32_t)(((uint64_t)1 << 32) / (uint64_t)tg.T[d] + 1) : 0u;
     }
-    tg.S2 = tg.T[2];
+    tg.S2 = tg.S4 = tg.T[2];
     if (dim == 3) plane_tap_order(tg, w);
+    set_no_halo(tg);
     return tg;
+}
+
+// Periodic halo that puts every tile box of a 3-D TMA interpolation (tile
+// origins o = bin * m - w/2, box [x0, x0 + B2) in the contiguous dimension
+// with x0 = o rounded down to even) inside the stored grid; false when a
+// halo would exceed a period.  lo[2] and hi[2] are even, so the padded rows
+// stay 16-byte multiples and x0 + lo[2] stays even (TMA alignment).
+bool grid_halo(const TileGeom& tg, GridHalo* h) {
+    if (tg.dim != 3) return false;
+    const int B2 = tma_box_x(tg);
+    for (int d = 0; d < 3; ++d) {
+        const int omax = (tg.nb[d] - 1) * tg.m[d] - tg.halfw;
+        int lo, hi;
+        if (d < 2) {
+            lo = tg.halfw;
+            hi = std::max(0, omax + tg.T[d] - tg.n[d]);
+        } else {
+            lo = tg.halfw + (tg.halfw & 1);
+            const int x0max = omax - (omax & 1);
+            hi = std::max(0, x0max + B2 - tg.n[d]);
+            hi += hi & 1;
+        }
+        if (lo + hi > tg.n[d]) return false;
+        h->lo[d] = lo;
+        h->hi[d] = hi;
+        h->P[d] = lo + tg.n[d] + hi;
+    }
+    return true;
+}
+
+void apply_halo(TileGeom& tg, const GridHalo& h) {
+    tg.pcells = 1;
+    for (int d = 0; d < 3; ++d) {
+        tg.lo[d] = h.lo[d];
+        tg.P[d] = h.P[d];
+        tg.pcells *= h.P[d];
+    }
 }
 
 // Caller-order chunk (points) of the bin sort.  In 1-D / 2-D a point touches
@@ -429,7 +495,7 @@ void alloc_grids(nufft_plan_s* p) {
     p->gfft = nullptr;
     dfree(p->gspread);
     p->gspread = nullptr;
-    p->gfft = (float2*)dmalloc(fft_cell_bytes(p) * p->nupcells * p->nbatch,
+    p->gfft = (float2*)dmalloc(fft_cell_bytes(p) * p->gcells * p->nbatch,
                                "fine grid");
     if (p->type == 3)
         p->gspread = (float2*)dmalloc(sizeof(float2) * p->nfcells * p->nbatch,
@@ -512,7 +578,10 @@ void create_t12(nufft_plan_s* p) {
         upload_dec(p, d, v);
     }
     p->tg_src = make_tile(p->dim, p->nup, p->w, p->beta, p->opts.kerevalmeth,
-                          p->type == 2);
+                          p->type == 2, (!p->fft64 && p->w <= 7) ? 12 : 10);
+    p->halo = p->type == 2 && halo_wanted(p) && grid_halo(p->tg_src, &p->gh);
+    if (p->halo) apply_halo(p->tg_src, p->gh);
+    p->gcells = p->halo ? p->tg_src.pcells : p->nupcells;
     p->nvg_src = vectors_per_tile(p->tg_src, p->nbatch);
     alloc_grids(p);
     p->sized = true;
@@ -559,6 +628,17 @@ void setpts_t12(nufft_plan_s* p, int64_t M, const double* const* xs,
                    p->type == 1 ? kMsubSpread : interp_msub(p->dim), p->type == 2,
                    pp, p->d_err, st);
     check_err_flag(p, st);
+    p->xneed_all = true;
+    if (p->halo && p->src.tiled) {
+        const int P0 = p->gh.P[0];
+        if (!p->xneed) p->xneed = (uint8_t*)dmalloc(P0, "plane marks");
+        NUFFT_CUDA(cudaMemsetAsync(p->xneed, 0, P0, st));
+        mark_tile_planes(p->src, p->tg_src, p->xneed, st);
+        std::vector<uint8_t> h(P0);
+        NUFFT_CUDA(cudaMemcpyAsync(h.data(), p->xneed, P0, cudaMemcpyDeviceToHost, st));
+        NUFFT_CUDA(cudaStreamSynchronize(st));
+        for (int i = 0; i < P0; ++i) p->xneed_all &= h[i] != 0;
+    }
     p->points_set = true;
 }
 
@@ -618,6 +698,7 @@ void size_t3(nufft_plan_s* p, const double* slo, const double* shi) {
         p->nfcells *= p->nf[d];
         p->nupcells *= p->nup[d];
     }
+    p->gcells = p->nupcells;
     // mode corrections (-1)^q / phihat2(2 pi q / n_up), q in [-nf/2, nf/2)
     std::vector<double> dq, aq;
     kernel_ft_nodes(p->beta2, p->w2, &dq, &aq);
@@ -788,11 +869,11 @@ const CUtensorMap* interp_tmap(nufft_plan_s* p, const TileGeom& tg) {
     static const int on = env_int("NUFFT_INTERP_TMA", 1);
     if (!on || p->fft64 || tg.dim != 3) return nullptr;
     if (p->tmap_grid != p->gfft || p->tmap_nbatch != p->nbatch ||
-        p->tmap_n[0] != tg.n[0] || p->tmap_n[1] != tg.n[1] || p->tmap_n[2] != tg.n[2]) {
+        p->tmap_n[0] != tg.P[0] || p->tmap_n[1] != tg.P[1] || p->tmap_n[2] != tg.P[2]) {
         p->tmap_ok = make_grid_tmap(&p->tmap, p->gfft, tg, p->nbatch);
         p->tmap_grid = p->gfft;
         p->tmap_nbatch = p->nbatch;
-        for (int d = 0; d < 3; ++d) p->tmap_n[d] = tg.n[d];
+        for (int d = 0; d < 3; ++d) p->tmap_n[d] = tg.P[d];
     }
     return p->tmap_ok ? &p->tmap : nullptr;
 }
@@ -826,6 +907,16 @@ bool use_fft1(nufft_plan_s* p) {
 bool fftn_wanted(const nufft_plan_s* p) {
     static const int on = env_int("NUFFT_FFTN", 1);
     return on && p->type != 3 && p->dim == 3 && !p->fft64 && fftn_supported(p->nup);
+}
+
+// A type-2 plan stores its FFT grid with a periodic halo when the pruned
+// 3-D FFT writes it (complex64) and the TMA interpolation reads it; every
+// 3-D interpolation kernel reads the halo layout.  NUFFT_GRID_HALO=0 keeps
+// the plain layout (tuning).
+bool halo_wanted(const nufft_plan_s* p) {
+    static const int on = env_int("NUFFT_GRID_HALO", 1);
+    static const int tma = env_int("NUFFT_INTERP_TMA", 1);
+    return on && tma && p->type == 2 && fftn_wanted(p);
 }
 
 bool use_fftn(nufft_plan_s* p) {
@@ -882,7 +973,9 @@ void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
                 fft1_rows(&p->fft1, p->gfft, 0, nullptr, nv, inv, st);
             } else if (use_fftn(p)) {  // pruned FFT with the pad fused
                 record(p, 1, st);
-                fftn_pad(&p->fftn, in, p->dec, p->gfft, nv, inv, st);
+                fftn_pad(&p->fftn, in, p->dec, p->gfft, nv, inv, st,
+                         p->halo ? &p->gh : nullptr,
+                         (stage == NUFFT_STAGE_ALL && !p->xneed_all) ? p->xneed : nullptr);
             } else {
                 launch_pad(p->dim, p->N, p->nup, p->dec, in, p->gfft, p->fft64, nv,
                            st);
@@ -965,7 +1058,10 @@ void adjoint_chunk_t12(nufft_plan_s* p, const float2* in, float2* out, int nv,
         sg = p->gadj;
     }
     NUFFT_CUDA(cudaMemsetAsync(sg, 0, sizeof(float2) * p->nupcells * nv, st));
-    launch_spread(p->src, p->tg_src, p->w, in, p->src.M, nv, sg, p->nvg_src, st);
+    // the adjoint spreads into plain (halo-free) grids for the crop
+    TileGeom tg = p->tg_src;
+    set_no_halo(tg);
+    launch_spread(p->src, tg, p->w, in, p->src.M, nv, sg, p->nvg_src, st);
     if (f1) {
         fft1_cols(&p->fft1, sg, 0, nullptr, nv, inv, st);
         fft1_rows(&p->fft1, out, p->N[0], p->dec[0], nv, inv, st);
@@ -1017,7 +1113,7 @@ void ensure_batch(nufft_plan_s* p, int nvec) {
     if (nvec <= p->nbatch || p->opts.max_batch > 0) return;
     size_t free_b = 0, tot = 0;
     NUFFT_CUDA(cudaMemGetInfo(&free_b, &tot));
-    size_t per = fft_cell_bytes(p) * (size_t)p->nupcells;
+    size_t per = fft_cell_bytes(p) * (size_t)p->gcells;
     if (p->type == 3) per += sizeof(float2) * (size_t)p->nfcells;
     else if (p->type == 1 && p->fft64) per += sizeof(float2) * (size_t)p->nupcells;
     if (fft1_wanted(p)) per += sizeof(float2) * (size_t)p->nupcells;  // FFT scratch
@@ -1274,7 +1370,7 @@ int nufft_get_grid(nufft_plan_t p, void** grid, int64_t* n_complex) {
         // the complex64 spreading target (type 1: what SPREAD leaves for a
         // cross-GPU reduction before FINISH)
         if (grid) *grid = p->type == 1 ? t1_spread_grid(p) : p->gfft;
-        if (n_complex) *n_complex = p->nupcells * p->nbatch;
+        if (n_complex) *n_complex = (p->type == 1 ? p->nupcells : p->gcells) * p->nbatch;
     });
 }
 
@@ -1344,6 +1440,7 @@ int nufft_plan_destroy(nufft_plan_t p) {
         for (int d = 0; d < 3; ++d) dfree(p->dec[d]);
         dfree(p->gfft);
         dfree(p->gspread);
+        dfree(p->xneed);
         dfree(p->d_ftd);
         dfree(p->d_fta);
         dfree(p->d_err);
@@ -1409,6 +1506,12 @@ int nufft_plan_get_info(nufft_plan_t p, nufft_plan_info* info) {
         info->fft_execs = p->fft_execs;
         info->fft64 = p->fft64 ? 1 : 0;
         info->fft_own = (fft1_wanted(p) || fftn_wanted(p)) ? 1 : 0;
+        info->grid_cells = p->type == 1 ? p->nupcells : p->gcells;
+        for (int d = 0; d < 3; ++d) {
+            const bool h = p->type == 2 && p->halo && d < p->dim;
+            info->grid_ext[d] = h ? p->gh.P[d] : (d < p->dim ? p->nup[d] : 1);
+            info->grid_lo[d] = h ? p->gh.lo[d] : 0;
+        }
     });
 }
 

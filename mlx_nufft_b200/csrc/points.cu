@@ -230,9 +230,10 @@ __device__ uint32_t block_exclusive_scan(uint32_t* a, int n, uint32_t* warp_tot)
     return total;
 }
 
-// Ranks inside residue classes: entries e = 0..n-1 hold a residue key[e] in
-// 0..15; afterwards key[e] = r | k << 4 with k the number of earlier
-// entries of residue r, and rcount[r] the entries of residue r.  A ballot
+// Ranks inside residue classes: entries e = 0..n-1 hold a residue in bits
+// 0..3 of key[e] (bits 17 and up are kept as they are); afterwards bits
+// 4..16 hold k, the number of earlier entries of the same residue (n <=
+// 8192), and rcount[r] counts the entries of residue r.  A ballot
 // multi-split over 256 entries at a time.
 __device__ void residue_ranks(uint32_t* key, int n, uint32_t* rcount,
                               uint32_t (*wres)[16]) {
@@ -243,7 +244,8 @@ __device__ void residue_ranks(uint32_t* key, int n, uint32_t* rcount,
         __syncthreads();
         const int pe = base + threadIdx.x;
         const bool act = pe < n;
-        const uint32_t r = act ? key[pe] : 16u;           // 16: no residue
+        const uint32_t kv = act ? key[pe] : 16u;
+        const uint32_t r = act ? (kv & 15u) : 16u;        // 16: no residue
         const unsigned mask = __match_any_sync(0xffffffffu, r);
         const uint32_t below = (uint32_t)__popc(mask & ((1u << lane) - 1u));
         if (act && below == 0) wres[wid][r] = (uint32_t)__popc(mask);
@@ -251,7 +253,7 @@ __device__ void residue_ranks(uint32_t* key, int n, uint32_t* rcount,
         if (act) {
             uint32_t k = rcount[r] + below;
             for (int w = 0; w < wid; ++w) k += wres[w][r];
-            key[pe] = r | (k << 4);
+            key[pe] = (kv & ~0x1ffffu) | r | (k << 4);
         }
         __syncthreads();
         if (threadIdx.x < 16) {
@@ -263,17 +265,80 @@ __device__ void residue_ranks(uint32_t* key, int n, uint32_t* rcount,
     }
 }
 
-// Rank of (k, r) in lexicographic order among the entries counted in
-// rcount: sum_{r'} min(n_{r'}, k) + #{r' < r : n_{r'} > k}.
-__device__ __forceinline__ uint32_t lex_rank(uint32_t kr, const uint32_t* rcount) {
-    const uint32_t r = kr & 15u, k = kr >> 4;
-    uint32_t pos = 0;
+// Greedy grouping of a subproblem's n points into rows of 16 consecutive
+// output positions (the half-warps of the interpolation kernels, one point
+// per lane) with as few repeated residues per row as the residue counts
+// allow: a row costs as many shared-memory wavefronts per tap load as its
+// most repeated residue, so the total is at least max(rows, max_r n_r).
+// Each row takes one point from each residue that has points left, largest
+// remainders first, passing over them again while the row has room (a
+// residue repeats in a row only once fewer than 16 residues remain).
+//
+// While all 16 residues have points and rows are full, every row takes
+// residue r into slot r: that happens for the first m = min(min_r n_r,
+// n / 16) rows only, so the k-th point of residue r with k < m goes to
+// position 16 k + r (computed by the caller).  This warp (lane r < 16
+// owning residue r, rcount[r] points in their rank order k) deals the rest
+// row by row and writes pos[rpre[r] + k - m] for k >= m, rpre being the
+// exclusive prefix of n_r - m (also written, with *s_m = m).
+__device__ void deal_rows(const uint32_t* rcount, uint32_t* rpre, uint32_t* pos,
+                          int n, int* s_m) {
+    const unsigned full = 0xffffffffu;
+    const int lane = threadIdx.x & 31;
+    const bool own = lane < 16;
+    const int nr = own ? (int)rcount[lane] : 0;
+    int m = 0;
+    if (__popc(__ballot_sync(full, own && nr > 0)) == 16) {
+        int mn = own ? nr : 0x7fffffff;
 #pragma unroll
-    for (int q = 0; q < 16; ++q) {
-        const uint32_t n = rcount[q];
-        pos += min(n, k) + ((uint32_t)q < r && n > k ? 1u : 0u);
+        for (int d = 16; d > 0; d >>= 1) mn = min(mn, __shfl_xor_sync(full, mn, d));
+        m = min(mn, n / 16);
     }
-    return pos;
+    const int nt = own ? nr - m : 0;
+    int pre = nt;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int v = __shfl_up_sync(full, pre, d);
+        if (lane >= d) pre += v;
+    }
+    pre -= nt;
+    if (own) rpre[lane] = (uint32_t)pre;
+    if (lane == 0) *s_m = m;
+    int taken = 0;                       // tail points of this residue dealt
+    for (int g = m, placed = 16 * m; placed < n; ++g) {
+        const int cap = min(16, n - 16 * g);
+        int t = 0, need = cap;
+        while (need > 0) {
+            const int r2 = nt - taken - t;
+            const bool av = own && r2 > 0;
+            const unsigned am = __ballot_sync(full, av);
+            const int c = __popc(am);
+            if (c == 0) break;           // never: rows hold no more than the points left
+            if (c <= need) {
+                t += av ? 1 : 0;
+                need -= c;
+            } else {
+                int rank = 0;            // among available residues, r2 descending
+                for (int j = 0; j < 16; ++j) {
+                    const int rj = __shfl_sync(full, r2, j);
+                    rank += (((am >> j) & 1u) && (rj > r2 || (rj == r2 && j < lane))) ? 1 : 0;
+                }
+                if (av && rank < need) t += 1;
+                need = 0;
+            }
+        }
+        int sp = t;                      // slot of this residue's first point in the row
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int v = __shfl_up_sync(full, sp, d);
+            if (lane >= d) sp += v;
+        }
+        sp -= t;
+        if (own)
+            for (int i = 0; i < t; ++i) pos[pre + taken + i] = (uint32_t)(16 * g + sp + i);
+        taken += t;
+        placed += cap;
+    }
 }
 
 // Order the points of every subproblem by their cell inside the bin
@@ -286,12 +351,14 @@ __device__ __forceinline__ uint32_t lex_rank(uint32_t kr, const uint32_t* rcount
 //  2. (interleave) residue r = (sum_d l_d rs[d]) mod 16 of the point's
 //     tile index; k = rank of the point among the residue-r points in cell
 //     order (a ballot multi-split);
-//  3. the output position is the rank of (k, r) in lexicographic order,
-//     so every run of 16 consecutive points (a half-warp of the
-//     interpolation kernels, one point per lane) holds 16 distinct residues
-//     wherever the buckets allow, and the lanes' 8-byte tap loads hit 16
-//     distinct bank pairs.
-// Shared memory: (cells per bin + 2 msub) x 4 bytes.
+//  3. one warp deals the residues into rows of 16 output positions (a
+//     half-warp of the interpolation kernels, one point per lane) with
+//     distinct residues wherever the counts allow (deal_rows), so the
+//     lanes' 8-byte tap loads hit distinct bank pairs.
+// Shared memory: (cells per bin + 2 msub) x 4 bytes with the residue
+// order (the per-point slots are reused for the dealt positions once each
+// cell-order entry carries its point's index), (cells per bin + msub) x 4
+// without.
 template <int DIM>
 __global__ void __launch_bounds__(256)
 k_sub_sort(const int4* __restrict__ subs, CellParams cp, int mcells, int msub,
@@ -302,9 +369,13 @@ k_sub_sort(const int4* __restrict__ subs, CellParams cp, int mcells, int msub,
     extern __shared__ uint32_t sm[];
     uint32_t* hist = sm;              // mcells counters, then starts
     uint32_t* slot = sm + mcells;     // per point: local cell | rank << 16
-    uint32_t* kres = slot + msub;     // per cell-order position: residue, then r | k << 4
+    // per cell-order position: residue | point << 17, then with k << 4 too
+    uint32_t* kres = slot + msub;
+    uint32_t* pos = slot;             // then: per (residue, rank) output position
     __shared__ uint32_t warp_tot[8];
     __shared__ uint32_t rcount[16];
+    __shared__ uint32_t rpre[16];
+    __shared__ int s_m;
     __shared__ uint32_t wres[8][16];
     const bool inter = cp.rs[0] != 0 || cp.rs[1] != 0 || cp.rs[2] != 0;
     const int4 sb = subs[blockIdx.x];
@@ -357,17 +428,21 @@ k_sub_sort(const int4* __restrict__ subs, CellParams cp, int mcells, int msub,
         }
         return;
     }
-    // cell-order position c of every point and its residue
+    // cell-order position c of every point: its residue and index there
     for (int t = threadIdx.x; t < cnt; t += blockDim.x) {
         const uint32_t sl = slot[t];
         const uint32_t c = hist[sl & 0xffffu] + (sl >> 16);
-        kres[c] = residue(t);
-        slot[t] = c;
+        kres[c] = residue(t) | ((uint32_t)t << 17);
     }
     __syncthreads();
-    residue_ranks(kres, cnt, rcount, wres);
-    for (int t = threadIdx.x; t < cnt; t += blockDim.x)
-        put(t, (int)lex_rank(kres[slot[t]], rcount));
+    residue_ranks(kres, cnt, rcount, wres);   // (also orders slot[] reads before pos[] writes)
+    if (threadIdx.x < 32) deal_rows(rcount, rpre, pos, cnt, &s_m);
+    __syncthreads();
+    const uint32_t m = (uint32_t)s_m;
+    for (int c = threadIdx.x; c < cnt; c += blockDim.x) {
+        const uint32_t kr = kres[c], r = kr & 15u, k = (kr >> 4) & 0x1fffu;
+        put((int)(kr >> 17), (int)(k < m ? 16u * k + r : pos[rpre[r] + k - m]));
+    }
 }
 
 // Type-3 phases, written in sorted order (position j reads caller index
@@ -521,7 +596,8 @@ void sub_sort(PointSet* ps, const CellParams& cp, int msub, cudaStream_t st) {
     const bool inter = c2.rs[0] != 0 || c2.rs[1] != 0 || c2.rs[2] != 0;
     int mcells = 1;
     for (int d = 0; d < DIM; ++d) mcells *= cp.m[d];
-    if (mcells > 65536 || msub > 65536) return;   // 16-bit slot fields
+    // 16-bit slot fields; 13-bit rank and point fields of the residue keys
+    if (mcells > 65536 || msub > 65536 || (inter && msub > 8192)) return;
     const size_t smem = sizeof(uint32_t) *
                         ((size_t)mcells + (size_t)msub * (inter ? 2 : 1));
     // opt in beyond the default dynamic limit (the kernel also has about

@@ -72,15 +72,17 @@ void ensure_smem(const void* kernel, size_t bytes) {
 
 namespace {
 
-constexpr size_t kPlaneTileBudget = 96 * 1024;
+// Shared memory (tile + staging) of one plane-spread CTA: two CTAs per SM.
+constexpr size_t kPlaneSmemBudget = 112 * 1024;
 
 // 3-D plane-owned spreading of NV vectors per launch.
-template <int W, int NV>
+template <int W, int NV, bool PRE>
 void launch_planes(const PointSet& ps, const TileGeom& tg, const float2* c,
                    int64_t cstride, const uint32_t* perm, const CellPtrs& cells,
                    float2* grid, cudaStream_t st) {
-    auto k = k_spread_planes<W, NV>;
-    const size_t smem = (size_t)NV * tg.T[0] * tg.T[1] * tg.S2 * sizeof(float2);
+    auto k = k_spread_planes<W, NV, PRE>;
+    const int S = (NUFFT_PLANE_PAIR && NV % 2 == 0) ? tg.S4 : tg.S2;
+    const size_t smem = (size_t)NV * tg.T[0] * tg.T[1] * S * sizeof(float2);
     ensure_smem((const void*)k, smem);
     const int blocks = persistent_grid((const void*)k, smem, ps.nsub,
                                        32 * kPlaneWarps);
@@ -99,24 +101,49 @@ void spread_impl(const PointSet& ps, const TileGeom& tg, const float2* c,
     if (ps.tiled) {
         if (ps.nsub == 0) return;
         if constexpr (DIM == 3 && W <= 10) {
-            // groups of 8, 4, 2 or 1 vectors, each group's tile within the
-            // budget (NUFFT_PLANE_KB overrides it, tuning)
+            // groups of 8, 4, 2 or 1 vectors: the most vectors whose tiles
+            // and staging fit the budget, with the staged weight products
+            // (W <= 8) when they fit too (NUFFT_PLANE_KB overrides the
+            // budget, NUFFT_PLANE_PRE=0 turns the products off; tuning)
             static const size_t budget = [] {
                 const char* e = std::getenv("NUFFT_PLANE_KB");
-                return (e && *e) ? (size_t)std::atoi(e) * 1024 : kPlaneTileBudget;
+                return (e && *e) ? (size_t)std::atoi(e) * 1024 : kPlaneSmemBudget;
             }();
-            const size_t per = (size_t)tg.T[0] * tg.T[1] * tg.S2 * sizeof(float2);
+            static const bool pre_on = [] {
+                const char* e = std::getenv("NUFFT_PLANE_PRE");
+                return !(e && *e && std::atoi(e) == 0);
+            }();
+            auto fits = [&](int nv, bool pre) {
+                const int S = (NUFFT_PLANE_PAIR && nv % 2 == 0) ? tg.S4 : tg.S2;
+                const size_t per = (size_t)tg.T[0] * tg.T[1] * S * sizeof(float2);
+                return nv * per + plane_static_bytes(W, nv, pre) <= budget;
+            };
             for (int v0 = 0; v0 < nvec;) {
                 const int left = nvec - v0;
-                const int nv = (left >= 8 && 8 * per <= budget) ? 8
-                             : (left >= 4 && 4 * per <= budget) ? 4
-                             : (left >= 2 && 2 * per <= budget) ? 2 : 1;
+                int nv = 1;
+                for (int cand : {8, 4, 2}) {
+                    if (left >= cand && fits(cand, false)) {
+                        nv = cand;
+                        break;
+                    }
+                }
+                const bool pre = pre_on && W <= 8 && fits(nv, true);
                 const float2* cv = c + v0 * cstride;
                 float2* gv = grid + v0 * tg.ncells;
-                if (nv == 8) launch_planes<W, 8>(ps, tg, cv, cstride, perm, cells, gv, st);
-                else if (nv == 4) launch_planes<W, 4>(ps, tg, cv, cstride, perm, cells, gv, st);
-                else if (nv == 2) launch_planes<W, 2>(ps, tg, cv, cstride, perm, cells, gv, st);
-                else launch_planes<W, 1>(ps, tg, cv, cstride, perm, cells, gv, st);
+                if constexpr (W <= 8) {
+                    if (pre) {
+                        if (nv == 8) launch_planes<W, 8, true>(ps, tg, cv, cstride, perm, cells, gv, st);
+                        else if (nv == 4) launch_planes<W, 4, true>(ps, tg, cv, cstride, perm, cells, gv, st);
+                        else if (nv == 2) launch_planes<W, 2, true>(ps, tg, cv, cstride, perm, cells, gv, st);
+                        else launch_planes<W, 1, true>(ps, tg, cv, cstride, perm, cells, gv, st);
+                        v0 += nv;
+                        continue;
+                    }
+                }
+                if (nv == 8) launch_planes<W, 8, false>(ps, tg, cv, cstride, perm, cells, gv, st);
+                else if (nv == 4) launch_planes<W, 4, false>(ps, tg, cv, cstride, perm, cells, gv, st);
+                else if (nv == 2) launch_planes<W, 2, false>(ps, tg, cv, cstride, perm, cells, gv, st);
+                else launch_planes<W, 1, false>(ps, tg, cv, cstride, perm, cells, gv, st);
                 v0 += nv;
             }
             return;

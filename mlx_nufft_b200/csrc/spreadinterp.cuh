@@ -162,6 +162,8 @@ __device__ __forceinline__ int wrap_tile(int x, int n) {
 // Global linear cell of tile index q (row-major over T, last dimension
 // fastest), with periodic wrap.  q / T[d] by multiply-high with the
 // plan's reciprocal tdiv[d] = ceil(2^32 / T[d]) (exact for q T[d] < 2^32).
+// 3-D: in the grid's stored layout (halo offsets lo, extents P; without a
+// halo lo = 0 and P = n).
 template <int DIM>
 __device__ __forceinline__ int64_t tile_to_global(int q, const int* o,
                                                   const TileGeom& tg) {
@@ -177,9 +179,9 @@ __device__ __forceinline__ int64_t tile_to_global(int q, const int* o,
         const int x = q - r * tg.T[2];
         const int z = (int)__umulhi((unsigned)r, tg.tdiv[1]);
         const int y = r - z * tg.T[1];
-        return ((int64_t)wrap_tile(o[0] + z, tg.n[0]) * tg.n[1] +
-                wrap_tile(o[1] + y, tg.n[1])) * tg.n[2] +
-               wrap_tile(o[2] + x, tg.n[2]);
+        return ((int64_t)(wrap_tile(o[0] + z, tg.n[0]) + tg.lo[0]) * tg.P[1] +
+                wrap_tile(o[1] + y, tg.n[1]) + tg.lo[1]) * tg.P[2] +
+               wrap_tile(o[2] + x, tg.n[2]) + tg.lo[2];
     }
 }
 
@@ -360,7 +362,24 @@ __host__ __device__ constexpr int batch_u() {
 constexpr int kPlaneWarps = 8;
 constexpr int kPlaneChunk = 128;
 
-template <int W, int NV>
+// Static shared memory of k_spread_planes<W, NV, PRE> (bytes, within 64).
+__host__ __device__ constexpr size_t plane_static_bytes(int W, int NV, bool pre) {
+    return (size_t)kPlaneChunk *
+               (8 + 4 * (pre ? W : 3 * W) +
+                4 * (pre ? (((W * W) & 1) ? W * W : W * W + 1) : 1) + 8 * NV) +
+           64;
+}
+
+// Vector pairs (NUFFT_PLANE_PAIR, default 1; an even NV): the tile holds
+// two vectors per 16-byte cell ([NV/2][T0][T1][S4] float4), so a tap round
+// is one 16-byte load / store per pair instead of one 8-byte one per
+// vector: a quarter of the load / store instructions saved, and a round
+// with few active lanes (W^2 mod 32 taps) moves half the wavefronts.
+#ifndef NUFFT_PLANE_PAIR
+#define NUFFT_PLANE_PAIR 1
+#endif
+
+template <int W, int NV, bool PRE>
 __global__ void __launch_bounds__(32 * kPlaneWarps)
 k_spread_planes(const float2* __restrict__ c, int64_t cstride,
                 const uint32_t* __restrict__ perm, CellPtrs cells,
@@ -370,22 +389,33 @@ k_spread_planes(const float2* __restrict__ c, int64_t cstride,
     constexpr int W2 = W * W;
     constexpr int NR = (W2 + 31) / 32;               // rounds per plane
     static_assert(NR <= kMaxTapRounds, "tap table too small");
-    extern __shared__ float2 tile[];                 // [NV][T0][T1][S2]
-    __shared__ int s_l0[kPlaneChunk];                // l0z, tile offset of (l0z, l0y, l0x)
-    __shared__ int s_off[kPlaneChunk];
-    __shared__ float s_w[kPlaneChunk][3 * W];
-    __shared__ float2 s_c[kPlaneChunk][NV];
+    constexpr bool PAIR = NUFFT_PLANE_PAIR && NV % 2 == 0;
+    constexpr int NT = PAIR ? NV / 2 : NV;           // tiles (vector pairs or vectors)
+    // PRE: the staging thread also forms the W^2 in-plane weight products,
+    // so a lane reads one product per round instead of two factors (rows of
+    // an odd stride: the staging stores are conflict-free); it costs
+    // 4 W^2 bytes of shared memory per staged point
+    static_assert(!PRE || W <= 8, "weight products staged for W <= 8 only");
+    constexpr int WS = PRE ? ((W2 & 1) ? W2 : W2 + 1) : 1;
+    extern __shared__ __align__(16) float2 tile[];   // [NV][T0][T1][S2] or pairs
+    float4* tile4 = reinterpret_cast<float4*>(tile); // [NV/2][T0][T1][S4]
+    __shared__ int2 s_pos[kPlaneChunk];              // (l0z or -1, in-plane offset)
+    __shared__ float s_w[kPlaneChunk][PRE ? W : 3 * W];
+    __shared__ float s_wyx[kPlaneChunk][WS];
+    __shared__ __align__(16) float2 s_c[kPlaneChunk][NV];
     __shared__ int s_sub;
     const int T = tg.tcells;
-    const int S2 = tg.S2, TT = tg.T[1] * tg.S2;
-    const int TS = tg.T[0] * TT;                     // padded cells per vector
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    // this lane's (y, x) tap in each round and its offset inside a plane
+    const int S2 = PAIR ? tg.S4 : tg.S2, TT = tg.T[1] * S2;
+    const int TS = tg.T[0] * TT;                     // padded cells per tile
+    const uint8_t* tapmap = PAIR ? tg.tapmap4 : tg.tapmap;
+    const int wid = threadIdx.x >> 5;
+    // this lane's (y, x) tap in each round: its offset inside a plane and
+    // its index b * W + k among the in-plane taps
     int rb[NR], rk[NR], roff[NR];
     bool ract[NR];
 #pragma unroll
     for (int r = 0; r < NR; ++r) {
-        const int m = tg.tapmap[r * 32 + lane];
+        const int m = tapmap[r * 32 + (threadIdx.x & 31)];
         ract[r] = m != 0xff;
         rb[r] = ract[r] ? (m >> 4) : 0;
         rk[r] = ract[r] ? (m & 15) : 0;
@@ -398,75 +428,135 @@ k_spread_planes(const float2* __restrict__ c, int64_t cstride,
         const int start = sb.x, cnt = sb.y;
         int o[3] = {0, 0, 0};
         bin_origin<3>(sb.z, tg, o);
+        // The staging thread's global loads are issued early: cells,
+        // permutation and phase of the next chunk before this chunk's taps,
+        // its strengths (through the permutation) before the barrier that
+        // waits for the taps of the other warps.
+        int2 pcl[3];
+        int64_t psrc = 0;
+        float2 pph = make_float2(1.0f, 0.0f);
+        auto fetch = [&](int cb) {
+            if (threadIdx.x < min(kPlaneChunk, cnt - cb)) {
+                const int64_t j = start + cb + threadIdx.x;
+#pragma unroll
+                for (int d = 0; d < 3; ++d) pcl[d] = __ldg(cells.d[d] + j);
+                psrc = perm ? (int64_t)__ldg(perm + j) : j;
+                if (phase) pph = __ldg(phase + j);
+            }
+        };
+        fetch(0);
         for (int q = threadIdx.x; q < NV * TS; q += blockDim.x)
             tile[q] = make_float2(0.0f, 0.0f);
         for (int c0 = 0; c0 < cnt; c0 += kPlaneChunk) {
             const int n = min(kPlaneChunk, cnt - c0);
+            float2 pcv[NV];
+            if (threadIdx.x < n) {
+#pragma unroll
+                for (int v = 0; v < NV; ++v) pcv[v] = __ldg(c + v * cstride + psrc);
+            }
             __syncthreads();      // tile zeroed / previous chunk consumed
             if (threadIdx.x < n) {
                 const int p = threadIdx.x;
-                const int64_t j = start + c0 + p;
                 int l0[3];
                 bool ok = true;
+                float wt[3][W];
 #pragma unroll
                 for (int d = 0; d < 3; ++d) {
-                    const int2 cl = __ldg(cells.d[d] + j);
+                    const int2 cl = pcl[d];
                     l0[d] = cl.x - o[d];
                     ok &= (unsigned)l0[d] < (unsigned)tg.m[d];
-                    float wt[W];
-                    kernel_weights<W>(__int_as_float(cl.y), tg, wt);
+                    kernel_weights<W>(__int_as_float(cl.y), tg, wt[d]);
+                }
+                if constexpr (PRE) {
 #pragma unroll
-                    for (int l = 0; l < W; ++l) s_w[p][d * W + l] = wt[l];
+                    for (int l = 0; l < W; ++l) s_w[p][l] = wt[0][l];
+#pragma unroll
+                    for (int b = 0; b < W; ++b)
+#pragma unroll
+                        for (int k = 0; k < W; ++k) s_wyx[p][b * W + k] = wt[1][b] * wt[2][k];
+                } else {
+#pragma unroll
+                    for (int d = 0; d < 3; ++d)
+#pragma unroll
+                        for (int l = 0; l < W; ++l) s_w[p][d * W + l] = wt[d][l];
                 }
                 // l0z = -1 marks a point outside the bin (never for
                 // consistent setpts output): every warp skips it
-                s_l0[p] = ok ? l0[0] : -1;
-                s_off[p] = l0[1] * S2 + l0[2];
-                const int64_t src = perm ? (int64_t)__ldg(perm + j) : j;
-                const float2 ph = phase ? __ldg(phase + j) : make_float2(1.0f, 0.0f);
+                s_pos[p] = make_int2(ok ? l0[0] : -1, l0[1] * S2 + l0[2]);
 #pragma unroll
-                for (int v = 0; v < NV; ++v) {
-                    float2 cv = __ldg(c + v * cstride + src);
-                    if (phase) cv = cmul(cv, ph);
-                    s_c[p][v] = cv;
-                }
+                for (int v = 0; v < NV; ++v) s_c[p][v] = phase ? cmul(pcv[v], pph) : pcv[v];
             }
             __syncthreads();
+            if (c0 + kPlaneChunk < cnt) fetch(c0 + kPlaneChunk);
             for (int p = 0; p < n; ++p) {
-                const int l0z = s_l0[p];
+                const int2 pos = s_pos[p];
+                const int l0z = pos.x;
                 if (l0z < 0) continue;
                 // planes z = l0z + a owned by this warp: a = (wid - l0z) mod 8
                 for (int a = (wid - l0z) & (kPlaneWarps - 1); a < W; a += kPlaneWarps) {
                     const float wa = s_w[p][a];
-                    const int base = (l0z + a) * TT + s_off[p];
+                    const int base = (l0z + a) * TT + pos.y;
                     float2 cv[NV];
+                    if constexpr (NV % 2 == 0) {
+                        const float4* c4 = reinterpret_cast<const float4*>(&s_c[p][0]);
 #pragma unroll
-                    for (int v = 0; v < NV; ++v) {
-                        const float2 cc = s_c[p][v];
-                        cv[v] = make_float2(cc.x * wa, cc.y * wa);
+                        for (int v = 0; v < NV / 2; ++v) {
+                            const float4 q = c4[v];
+                            cv[2 * v] = make_float2(q.x * wa, q.y * wa);
+                            cv[2 * v + 1] = make_float2(q.z * wa, q.w * wa);
+                        }
+                    } else {
+#pragma unroll
+                        for (int v = 0; v < NV; ++v) {
+                            const float2 cc = s_c[p][v];
+                            cv[v] = make_float2(cc.x * wa, cc.y * wa);
+                        }
                     }
                     float wr[NR];
                     int q[NR];
 #pragma unroll
                     for (int r = 0; r < NR; ++r) {
-                        wr[r] = s_w[p][W + rb[r]] * s_w[p][2 * W + rk[r]];
+                        if constexpr (PRE)
+                            wr[r] = s_wyx[p][rb[r] * W + rk[r]];
+                        else
+                            wr[r] = s_w[p][W + rb[r]] * s_w[p][2 * W + rk[r]];
                         q[r] = base + roff[r];
                     }
-                    float2 g[NR][NV];
+                    if constexpr (PAIR) {
+                        float4 g[NR][NT];
 #pragma unroll
-                    for (int r = 0; r < NR; ++r)
-                        if (ract[r])
+                        for (int r = 0; r < NR; ++r)
+                            if (ract[r])
 #pragma unroll
-                            for (int v = 0; v < NV; ++v) g[r][v] = tile[v * TS + q[r]];
+                                for (int v = 0; v < NT; ++v) g[r][v] = tile4[v * TS + q[r]];
 #pragma unroll
-                    for (int r = 0; r < NR; ++r)
-                        if (ract[r])
+                        for (int r = 0; r < NR; ++r)
+                            if (ract[r])
 #pragma unroll
-                            for (int v = 0; v < NV; ++v) {
-                                g[r][v].x = fmaf(cv[v].x, wr[r], g[r][v].x);
-                                g[r][v].y = fmaf(cv[v].y, wr[r], g[r][v].y);
-                                tile[v * TS + q[r]] = g[r][v];
-                            }
+                                for (int v = 0; v < NT; ++v) {
+                                    g[r][v].x = fmaf(cv[2 * v].x, wr[r], g[r][v].x);
+                                    g[r][v].y = fmaf(cv[2 * v].y, wr[r], g[r][v].y);
+                                    g[r][v].z = fmaf(cv[2 * v + 1].x, wr[r], g[r][v].z);
+                                    g[r][v].w = fmaf(cv[2 * v + 1].y, wr[r], g[r][v].w);
+                                    tile4[v * TS + q[r]] = g[r][v];
+                                }
+                    } else {
+                        float2 g[NR][NV];
+#pragma unroll
+                        for (int r = 0; r < NR; ++r)
+                            if (ract[r])
+#pragma unroll
+                                for (int v = 0; v < NV; ++v) g[r][v] = tile[v * TS + q[r]];
+#pragma unroll
+                        for (int r = 0; r < NR; ++r)
+                            if (ract[r])
+#pragma unroll
+                                for (int v = 0; v < NV; ++v) {
+                                    g[r][v].x = fmaf(cv[v].x, wr[r], g[r][v].x);
+                                    g[r][v].y = fmaf(cv[v].y, wr[r], g[r][v].y);
+                                    tile[v * TS + q[r]] = g[r][v];
+                                }
+                    }
                 }
                 __syncwarp();
             }
@@ -477,11 +567,22 @@ k_spread_planes(const float2* __restrict__ c, int64_t cstride,
             // shared index of tile cell q: row q / T2 at stride S2
             const int row = (int)__umulhi((unsigned)q, tg.tdiv[2]);
             const int sq = row * S2 + (q - row * tg.T[2]);
+            if constexpr (PAIR) {
 #pragma unroll
-            for (int v = 0; v < NV; ++v) {
-                const float2 val = tile[v * TS + sq];
-                if (val.x != 0.0f || val.y != 0.0f)
-                    atomicAdd(grid + v * tg.ncells + g, val);
+                for (int v = 0; v < NT; ++v) {
+                    const float4 val = tile4[v * TS + sq];
+                    if (val.x != 0.0f || val.y != 0.0f)
+                        atomicAdd(grid + 2 * v * tg.ncells + g, make_float2(val.x, val.y));
+                    if (val.z != 0.0f || val.w != 0.0f)
+                        atomicAdd(grid + (2 * v + 1) * tg.ncells + g, make_float2(val.z, val.w));
+                }
+            } else {
+#pragma unroll
+                for (int v = 0; v < NV; ++v) {
+                    const float2 val = tile[v * TS + sq];
+                    if (val.x != 0.0f || val.y != 0.0f)
+                        atomicAdd(grid + v * tg.ncells + g, val);
+                }
             }
         }
     }
@@ -595,7 +696,7 @@ k_interp_tiled(const G* __restrict__ grid, int nvg,
         for (int q = threadIdx.x; q < T; q += blockDim.x) {
             const int64_t g = tile_to_global<DIM>(q, o, tg);
             for (int v = 0; v < nvg; ++v)
-                tile[v * T + q] = load_cell(grid + v * tg.ncells + g);
+                tile[v * T + q] = load_cell(grid + v * tg.pcells + g);
         }
         __syncthreads();
         for (int base = 0; base < cnt; base += U * blockDim.x) {
@@ -643,6 +744,8 @@ k_interp_tiled(const G* __restrict__ grid, int nvg,
 
 // --------------------------------------------------------------------
 // global-memory variants: one thread per point (sorted or caller order).
+// Tap indices are in the grid's stored layout (lo, P; 3-D grids may carry
+// a periodic halo).
 template <int DIM, int W>
 __device__ __forceinline__ void global_taps(const CellPtrs& cells, int64_t j,
                                             const TileGeom& tg,
@@ -653,7 +756,7 @@ __device__ __forceinline__ void global_taps(const CellPtrs& cells, int64_t j,
         int2 cl = __ldg(cells.d[d] + j);
         kernel_weights<W>(__int_as_float(cl.y), tg, wgt[d]);
 #pragma unroll
-        for (int l = 0; l < W; ++l) idx[d][l] = wrap1(cl.x + l, tg.n[d]);
+        for (int l = 0; l < W; ++l) idx[d][l] = wrap1(cl.x + l, tg.n[d]) + tg.lo[d];
     }
 }
 
@@ -679,12 +782,12 @@ __device__ __forceinline__ void global_add(float2* gv, const TileGeom& tg,
     } else {
 #pragma unroll 1
         for (int a = 0; a < W; ++a) {
-            const int64_t plane = (int64_t)idx[0][0] * tg.n[1];
+            const int64_t plane = (int64_t)idx[0][0] * tg.P[1];
             const float wa = wgt[0][0];
 #pragma unroll
             for (int b = 0; b < W; ++b) {
                 const float wab = wa * wgt[1][b];
-                const int64_t base = (plane + idx[1][b]) * tg.n[2];
+                const int64_t base = (plane + idx[1][b]) * tg.P[2];
 #pragma unroll
                 for (int k = 0; k < W; ++k) {
                     const float wk = wab * wgt[2][k];
@@ -727,11 +830,11 @@ __device__ __forceinline__ float2 global_gather(const G* gv,
     } else {
 #pragma unroll 1
         for (int a = 0; a < W; ++a) {
-            const int64_t plane = (int64_t)idx[0][0] * tg.n[1];
+            const int64_t plane = (int64_t)idx[0][0] * tg.P[1];
             float2 sa = make_float2(0.0f, 0.0f);
 #pragma unroll
             for (int b = 0; b < W; ++b) {
-                const G* row = gv + (plane + idx[1][b]) * tg.n[2];
+                const G* row = gv + (plane + idx[1][b]) * tg.P[2];
                 float2 s = make_float2(0.0f, 0.0f);
 #pragma unroll
                 for (int k = 0; k < W; ++k) {
@@ -785,7 +888,7 @@ k_interp_global(const G* __restrict__ grid, int nvec,
     global_taps<DIM, W>(cells, j, tg, wgt, idx);
     const float2 ph = phase ? __ldg(phase + j) : make_float2(1.0f, 0.0f);
     for (int v = 0; v < nvec; ++v) {
-        float2 acc = global_gather<DIM, W, G>(grid + v * tg.ncells, tg, wgt, idx);
+        float2 acc = global_gather<DIM, W, G>(grid + v * tg.pcells, tg, wgt, idx);
         if (phase) acc = cmul(acc, ph);
         out[v * ostride + dst] = acc;
     }

@@ -87,15 +87,40 @@ class _DeviceArray:
             "data": (int(ptr), False), "version": 3, "strides": None}
 
 
-def plan_grid_view(native, n_up, nvec=1, fp64=False):
-    """The native plan's fine grid(s) as a (nvec, *n_up) complex CUDA tensor
-    sharing its memory (nufft_get_grid)."""
+def plan_grid_storage(native, nvec=1, fp64=False):
+    """The native plan's stored fine grid(s) as a contiguous (nvec, *ext)
+    complex CUDA tensor sharing its memory (nufft_get_grid; ext = the fine
+    grid's extents plus the periodic halo of a 3-D type-2 grid, the fine
+    grid itself otherwise): what a broadcast or reduction of the grid
+    moves."""
+    info = native.info()
     ptr, n = native.grid()
-    cells = int(np.prod(n_up))
+    cells = int(info.grid_cells)
     if nvec * cells > n:
         raise ValueError("plan grid holds fewer vectors than requested")
-    arr = _DeviceArray(ptr, (nvec,) + tuple(n_up), "<c16" if fp64 else "<c8")
+    ext = tuple(int(info.grid_ext[d]) for d in range(int(info.dim)))
+    arr = _DeviceArray(ptr, (nvec,) + ext, "<c16" if fp64 else "<c8")
     return torch.as_tensor(arr, device=torch.device("cuda", native.device))
+
+
+def plan_grid_view(native, n_up, nvec=1, fp64=False):
+    """The native plan's fine grid(s) as a (nvec, *n_up) complex CUDA tensor
+    sharing its memory: a strided view that skips the periodic halo of a
+    3-D type-2 grid (nufft_plan_info grid_ext / grid_lo)."""
+    info = native.info()
+    flat = plan_grid_storage(native, nvec, fp64)
+    if tuple(flat.shape[1:]) == tuple(int(v) for v in n_up):
+        return flat                                    # no halo
+    dim = len(n_up)
+    ext = [int(info.grid_ext[d]) for d in range(dim)]
+    lo = [int(info.grid_lo[d]) for d in range(dim)]
+    strides, acc = [], 1
+    for e in reversed(ext):
+        strides.insert(0, acc)
+        acc *= e
+    off = sum(l * st for l, st in zip(lo, strides))
+    return torch.as_strided(flat, (nvec,) + tuple(int(v) for v in n_up),
+                            (int(info.grid_cells),) + tuple(strides), off)
 
 
 class PlanStages:
@@ -110,8 +135,7 @@ class PlanStages:
         self.n_up = tuple(int(info.n_up[d]) for d in range(info.dim))
 
     def grid(self):
-        return plan_grid_view(self.native, self.n_up, 1,
-                              fp64=self.fp64 and self.type == 2)
+        return plan_grid_storage(self.native, 1, fp64=self.fp64 and self.type == 2)
 
     def first(self, data):
         d = as_c64(data, self.native.device).reshape(-1)

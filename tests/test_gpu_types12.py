@@ -197,11 +197,12 @@ def test_upsampfac_125_and_odd_sizes(rng):
 
 @pytest.mark.parametrize("N", [(64, 48, 40), (48, 64, 36)])
 def test_type2_3d_batch_tma_staged_tiles(N, rng):
-    """3-D type 2 over several vectors (TMA-staged tiles, one tensor-map
-    coordinate per vector; bins at the periodic edge loaded by hand): the
-    batch equals per-vector executes bit for bit (interpolation is
-    deterministic) and the direct sum within the gate; points cluster at
-    the grid corner so both tile paths carry dense bins."""
+    """3-D type 2 over several vectors on cuFFT-sized grids (no periodic
+    halo: TMA-staged tiles, one tensor-map coordinate per vector, and the
+    bins at the periodic edge loaded by hand): the batch equals per-vector
+    executes bit for bit (interpolation is deterministic) and the direct
+    sum within the gate; points cluster at the grid corner so both tile
+    paths carry dense bins."""
     from mlx_nufft_b200 import Type2PlanND
     P = 120_000
     x = [np.concatenate([rng.uniform(-np.pi, np.pi, P // 2),
@@ -224,11 +225,9 @@ def test_type2_3d_batch_tma_staged_tiles(N, rng):
 @pytest.mark.parametrize("isign", [-1, +1])
 def test_type2_3d_dense_point_pairs(isign, rng):
     """Dense 3-D interpolation subproblems (thousands of points per 10^3
-    bin, many points per cell): the sort pairs points of one cell and the
-    TMA-staged kernel gathers each pair in one pass over the taps (odd
-    cells leave single points, gathered two per thread, the last one
-    alone).  Every output against the fp64 restatement of the pipeline,
-    and a sample against the exact sum."""
+    bin, many points per cell, split into several subproblems of one bin),
+    with a sparse fringe.  Every output against the fp64 restatement of the
+    pipeline, and a sample against the exact sum."""
     from mlx_nufft_b200 import Type2PlanND
     N, M = (24, 20, 28), 300_001
     x = [np.mod(rng.normal(0, 0.25, M) + np.pi, 2 * np.pi) - np.pi for _ in range(3)]
@@ -242,3 +241,64 @@ def test_type2_3d_dense_point_pairs(isign, rng):
     assert port.rel_l2(c[idx], fast.direct_t2(x, fk, isign, idx)) <= gate(1e-6)
     # deterministic: a second execute is bit-identical
     np.testing.assert_array_equal(plan.execute(fk), c)
+
+
+@pytest.mark.parametrize("N,eps,isign", [((32, 32, 32), 1e-6, -1),
+                                         ((32, 64, 32), 1e-6, +1),
+                                         ((32, 32, 64), 1e-9, -1)])
+def test_type2_3d_halo_grid(N, eps, isign, rng):
+    """3-D type 2 on power-of-two fine grids: the pruned FFT writes the grid
+    with a periodic halo (the stage API reports more cells than the grid
+    has) and every tile is copied by TMA, none wraps.  Points half uniform,
+    half clustered at the periodic corner (where the halo copies are read),
+    two vectors: all outputs against the fp64 restatement of the pipeline,
+    a sample against the exact sum, batch equal to single executes."""
+    from mlx_nufft_b200 import Type2PlanND
+    P = 150_000
+    x = [np.concatenate([rng.uniform(-np.pi, np.pi, P // 2),
+                         np.mod(rng.normal(0, 0.3, P // 2) + np.pi, 2 * np.pi) - np.pi])
+         for _ in range(3)]
+    fks = (rng.standard_normal((2,) + N) + 1j * rng.standard_normal((2,) + N)
+           ).astype(np.complex64)
+    plan = Type2PlanND(tuple(x), N, eps=eps, isign=isign)
+    info = plan._plan.info()
+    assert info.tiled
+    nup = int(np.prod([int(info.n_up[d]) for d in range(3)]))
+    assert info.grid_cells > nup                       # halo in effect
+    _, ncomplex = plan._plan.grid()
+    assert ncomplex % info.grid_cells == 0
+    got = plan.execute_batch(fks)
+    idx = rng.choice(P, 200, replace=False)
+    for b in range(2):
+        np.testing.assert_array_equal(got[b], plan.execute(fks[b]))
+        assert port.rel_l2(got[b], port.nufft_t2(x, fks[b], eps, isign)) <= max(20 * eps, 2e-5)
+        exact = fast.direct_t2([v[idx] for v in x], fks[b], isign)
+        assert port.rel_l2(got[b][idx], exact) <= gate(eps)
+
+
+@pytest.mark.parametrize("lo,hi", [(-0.4, 0.5), (1.0, 1.6)])
+def test_type2_3d_slab_points_pruned_planes(lo, hi, rng):
+    """A 3-D type-2 plan whose points fill one slab of the first coordinate
+    (as each rank's share in the x-slab split of bench.py): setpts marks the
+    grid planes its tiles read and the execute's last FFT pass writes only
+    those (plus their halo copies).  The first slab straddles the periodic
+    seam at 0 (tiles at both ends of the grid).  The execute equals the
+    staged execute (whose grid is written whole) bit for bit, and the fp64
+    restatement of the pipeline within the gate."""
+    import torch
+    from mlx_nufft_b200 import Type2PlanND, _lib
+    N, P = (32, 32, 32), 100_000
+    x = [rng.uniform(lo, hi, P), rng.uniform(-np.pi, np.pi, P),
+         rng.uniform(-np.pi, np.pi, P)]
+    fk = (rng.standard_normal(N) + 1j * rng.standard_normal(N)).astype(np.complex64)
+    plan = Type2PlanND(tuple(x), N, eps=1e-6)
+    info = plan._plan.info()
+    assert info.tiled and info.grid_cells > np.prod([int(info.n_up[d]) for d in range(3)])
+    got = plan.execute(fk)
+    ft = torch.from_numpy(fk).cuda()
+    out = torch.empty(P, dtype=torch.complex64, device="cuda")
+    plan._plan.execute_stage(_lib.STAGE_SPREAD, ft, None, 1)
+    plan._plan.execute_stage(_lib.STAGE_FINISH, None, out, 1)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(got, out.cpu().numpy())
+    assert port.rel_l2(got, port.nufft_t2(x, fk, 1e-6, -1)) <= 2e-5
