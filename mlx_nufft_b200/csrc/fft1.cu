@@ -657,6 +657,124 @@ k_halo_fill(float2* __restrict__ G, int64_t G_vs, GridHalo h, int n0, int n1, in
     }
 }
 
+// ---------------------------------------------------------------------
+// Slab order of the pad, for a plan whose points read only some planes of
+// dimension 0 (one x-slab of the points per GPU): the X pass first, over
+// the N1 x N2 mode columns, keeping only the nx needed planes (xmap[x]:
+// compact index of fine plane x, or -1); then Y and Z over those planes
+// only.  The Z pass writes the interior of the halo-padded grid (plane
+// xlist[xi] at stored index xlist[xi] + lo[0]); k_halo_fill adds the
+// copies.  T1 [nx][N1][N2] and T2 [nx][n1][N2] are the scratch planes.
+
+// pass X: columns (m1, z0 + c) of the mode box; blockIdx.y = m1
+template <int L, bool INV>
+__global__ void __launch_bounds__(kFftThreads, NUFFT_FFTN_MINB)
+k_fftn_slab_x(const float2* __restrict__ f, int64_t f_vs, const float* __restrict__ d0,
+              const float* __restrict__ d1, const float* __restrict__ d2, int N0, int N1,
+              int N2, const int* __restrict__ xmap, const float2* __restrict__ twL,
+              float2* __restrict__ T1, int64_t T1_vs) {
+    constexpr int C = fftn_cols(L);
+    extern __shared__ float2 s[];
+    const int z0 = blockIdx.x * C;
+    const int m1 = blockIdx.y;
+    f += blockIdx.z * f_vs;
+    T1 += blockIdx.z * T1_vs;
+    const float dm1 = __ldg(d1 + m1);
+    auto load = [&](int c, int i) {
+        const int m = band_mode(i, L, N0), m2 = z0 + c;
+        if (m < 0 || m2 >= N2) return make_float2(0.0f, 0.0f);
+        const float d = __ldg(d0 + m) * dm1 * __ldg(d2 + m2);
+        const float2 g = __ldg(f + ((int64_t)m * N1 + m1) * N2 + m2);
+        return make_float2(g.x * d, g.y * d);
+    };
+    auto store = [&](int c, int base, int stride, auto& vals) {
+        const int m2 = z0 + c;
+        if (m2 >= N2) return;
+#pragma unroll
+        for (int k = 0; k < vals_len<decltype(vals)>(); ++k) {
+            const int xi = __ldg(xmap + base + k * stride);
+            if (xi >= 0) T1[((int64_t)xi * N1 + m1) * N2 + m2] = vals[k];
+        }
+    };
+    fft_stages_c<L, 1, INV, C>(s, twL, load, store);
+}
+
+// pass Y: columns (xi, z0 + c); blockIdx.y = xi
+template <int L, bool INV>
+__global__ void __launch_bounds__(kFftThreads, NUFFT_FFTN_MINB)
+k_fftn_slab_y(const float2* __restrict__ T1, int64_t T1_vs, int N1, int N2,
+              const float2* __restrict__ twL, float2* __restrict__ T2, int64_t T2_vs) {
+    constexpr int C = fftn_cols(L);
+    extern __shared__ float2 s[];
+    grid_dep_sync();
+    const int z0 = blockIdx.x * C;
+    const int64_t xi = blockIdx.y;
+    T1 += blockIdx.z * T1_vs;
+    T2 += blockIdx.z * T2_vs;
+    auto load = [&](int c, int i) {
+        const int m = band_mode(i, L, N1), m2 = z0 + c;
+        return (m >= 0 && m2 < N2) ? __ldg(T1 + (xi * N1 + m) * N2 + m2)
+                                   : make_float2(0.0f, 0.0f);
+    };
+    auto store = [&](int c, int base, int stride, auto& vals) {
+        const int m2 = z0 + c;
+        if (m2 >= N2) return;
+#pragma unroll
+        for (int k = 0; k < vals_len<decltype(vals)>(); ++k)
+            T2[(xi * L + base + k * stride) * N2 + m2] = vals[k];
+    };
+    fft_stages_c<L, 1, INV, C>(s, twL, load, store);
+}
+
+// pass Z: rows r = xi * n1 + y of T2 (N2 modes each, contiguous), padded to
+// L = n2, written as whole rows of the stored grid
+template <int L, bool INV>
+__global__ void __launch_bounds__(kFftThreads, NUFFT_FFTN_MINB)
+k_fftn_slab_z(const float2* __restrict__ T2, int64_t T2_vs, int N2, int nrows, int n1,
+              const int* __restrict__ xlist, GridHalo h, const float2* __restrict__ twL,
+              float2* __restrict__ G, int64_t G_vs) {
+    constexpr int C = fftn_cols(L);
+    extern __shared__ float2 s[];
+    __shared__ int64_t s_row[C];                 // stored-grid offset of each row
+    grid_dep_sync();
+    const int r0 = blockIdx.x * C;
+    const int rows = min(C, nrows - r0);
+    T2 += blockIdx.z * T2_vs + (int64_t)r0 * N2;
+    G += blockIdx.z * G_vs;
+    if (threadIdx.x < rows) {
+        const int r = r0 + threadIdx.x;
+        const int xi = r / n1, y = r - xi * n1;
+        s_row[threadIdx.x] = ((int64_t)(__ldg(xlist + xi) + h.lo[0]) * h.P[1] + y + h.lo[1]) *
+                                 h.P[2] + h.lo[2];
+    }
+    constexpr int K = 8;
+    for (int m = threadIdx.x; m < N2; m += kFftThreads) {
+        const int cell = ((m - N2 / 2 + L) % L) * C;
+        for (int c0 = 0; c0 < C; c0 += K) {
+            float2 x[K];
+#pragma unroll
+            for (int k = 0; k < K; ++k)
+                x[k] = c0 + k < rows ? __ldg(T2 + (int64_t)(c0 + k) * N2 + m)
+                                     : make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int k = 0; k < K; ++k) s[fpad(cell + c0 + k)] = x[k];
+        }
+    }
+    for (int q = threadIdx.x; q < C * (L - N2); q += kFftThreads) {
+        const int c = q % C, i = N2 - N2 / 2 + q / C;     // out-of-band fine cells
+        s[fpad(i * C + c)] = make_float2(0.0f, 0.0f);
+    }
+    __syncthreads();
+    auto none = [](int, int) { return make_float2(0.0f, 0.0f); };
+    auto nost = [](int, int, int, auto&) {};
+    fft_stages_c<L, 1, INV, C, true>(s, twL, none, nost);
+    __syncthreads();
+    for (int q = threadIdx.x; q < rows * L; q += kFftThreads) {
+        const int c = q / L, i = q - c * L;
+        G[s_row[c] + i] = s[fpad(i * C + c)];
+    }
+}
+
 // pass X of the crop: columns (y, z0 + c) of the full grid, in-band x only
 template <int L, bool INV>
 __global__ void __launch_bounds__(kFftThreads, NUFFT_FFTN_MINB)
@@ -833,6 +951,21 @@ void fftn_reserve(Fftn* f, int nv) {
     f->tmp_batch = nv;
 }
 
+// The periodic copies of k grids (stored layout h, G cells apart) from
+// their interior: three k_halo_fill passes (need: marked planes only).
+void halo_fill(float2* Gv, int64_t G, const GridHalo& h, int n0, int n1, int n2, int k,
+               const uint8_t* need, cudaStream_t st) {
+    const int64_t work[3] = {(int64_t)(h.lo[0] + h.hi[0]) * h.P[1] * h.P[2],
+                             (int64_t)n0 * (h.lo[1] + h.hi[1]) * h.P[2],
+                             (int64_t)n0 * n1 * (h.lo[2] + h.hi[2])};
+    for (int pass = 2; pass >= 0; --pass) {
+        if (work[pass] == 0) continue;
+        const dim3 g((unsigned)((work[pass] + 255) / 256), (unsigned)k);
+        k_halo_fill<<<g, 256, 0, st>>>(Gv, G, h, n0, n1, n2, pass, need);
+        NUFFT_LAUNCH("k_halo_fill");
+    }
+}
+
 void fftn_pad(Fftn* f, const float2* modes, const float* const* dec, float2* grid,
               int nv, bool inv, cudaStream_t st, const GridHalo* halo,
               const uint8_t* need) {
@@ -895,19 +1028,57 @@ void fftn_pad(Fftn* f, const float2* modes, const float* const* dec, float2* gri
             }
         });
         NUFFT_LAUNCH("k_fftn_pad_x");
-        if (halo) {
-            const int64_t work[3] = {
-                (int64_t)(h.lo[0] + h.hi[0]) * h.P[1] * h.P[2],
-                (int64_t)n0 * (h.lo[1] + h.hi[1]) * h.P[2],
-                (int64_t)n0 * n1 * (h.lo[2] + h.hi[2])};
-            for (int pass = 2; pass >= 0; --pass) {
-                if (work[pass] == 0) continue;
-                const dim3 g((unsigned)((work[pass] + 255) / 256), (unsigned)k);
-                k_halo_fill<<<g, 256, 0, st>>>(Gv, G, h, n0, n1, n2, pass, need);
-                NUFFT_LAUNCH("k_halo_fill");
-            }
-        }
+        if (halo) halo_fill(Gv, G, h, n0, n1, n2, k, need, st);
     }
+}
+
+bool fftn_pad_slab(Fftn* f, const float2* modes, const float* const* dec, float2* grid,
+                   int nv, bool inv, cudaStream_t st, const GridHalo& h,
+                   const uint8_t* need, const int* xmap, const int* xlist, int nx) {
+    const int n0 = f->n[0], n1 = f->n[1], n2 = f->n[2];
+    const int N0 = f->N[0], N1 = f->N[1], N2 = f->N[2];
+    const int64_t K = (int64_t)N0 * N1 * N2;
+    const int64_t G = (int64_t)h.P[0] * h.P[1] * h.P[2];
+    const int64_t Bs = fftn_scratch_cells(*f);
+    const int64_t t1 = (int64_t)nx * N1 * N2, t2 = (int64_t)nx * n1 * N2;
+    if (nx < 1 || t1 > G || t2 > Bs) return false;   // scratch planes do not fit
+    fftn_reserve(f, nv);
+    for (int v0 = 0; v0 < nv; v0 += 65535) {
+        const int k = std::min(65535, nv - v0);
+        const float2* fv = modes + v0 * K;
+        float2* T1 = grid + v0 * G;       // dead before the Z pass writes the grid
+        float2* T2 = f->tmp + v0 * Bs;
+        float2* Gv = grid + v0 * G;
+        NUFFT_FFT_LEN_SWITCH(n0, {
+            dim3 g((unsigned)((N2 + fftn_cols(L) - 1) / fftn_cols(L)), (unsigned)N1, (unsigned)k);
+            if (inv) fftn_launch(k_fftn_slab_x<L, true>, g, fftn_smem<L>(), st, false, fv, K,
+                                 dec[0], dec[1], dec[2], N0, N1, N2, xmap, fftn_tw(*f, 0), T1, G);
+            else fftn_launch(k_fftn_slab_x<L, false>, g, fftn_smem<L>(), st, false, fv, K,
+                             dec[0], dec[1], dec[2], N0, N1, N2, xmap, fftn_tw(*f, 0), T1, G);
+        });
+        NUFFT_LAUNCH("k_fftn_slab_x");
+        NUFFT_FFT_LEN_SWITCH(n1, {
+            dim3 g((unsigned)((N2 + fftn_cols(L) - 1) / fftn_cols(L)), (unsigned)nx, (unsigned)k);
+            if (inv) fftn_launch(k_fftn_slab_y<L, true>, g, fftn_smem<L>(), st, true,
+                                 (const float2*)T1, G, N1, N2, fftn_tw(*f, 1), T2, Bs);
+            else fftn_launch(k_fftn_slab_y<L, false>, g, fftn_smem<L>(), st, true,
+                             (const float2*)T1, G, N1, N2, fftn_tw(*f, 1), T2, Bs);
+        });
+        NUFFT_LAUNCH("k_fftn_slab_y");
+        NUFFT_FFT_LEN_SWITCH(n2, {
+            const int nrows = nx * n1;
+            dim3 g((unsigned)((nrows + fftn_cols(L) - 1) / fftn_cols(L)), 1u, (unsigned)k);
+            if (inv) fftn_launch(k_fftn_slab_z<L, true>, g, fftn_smem<L>(), st, true,
+                                 (const float2*)T2, Bs, N2, nrows, n1, xlist, h,
+                                 fftn_tw(*f, 2), Gv, G);
+            else fftn_launch(k_fftn_slab_z<L, false>, g, fftn_smem<L>(), st, true,
+                             (const float2*)T2, Bs, N2, nrows, n1, xlist, h,
+                             fftn_tw(*f, 2), Gv, G);
+        });
+        NUFFT_LAUNCH("k_fftn_slab_z");
+        halo_fill(Gv, G, h, n0, n1, n2, k, need, st);
+    }
+    return true;
 }
 
 void fftn_crop(Fftn* f, float2* grid, const float* const* dec, float2* modes, int nv,

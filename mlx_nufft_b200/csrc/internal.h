@@ -256,6 +256,14 @@ int64_t fftn_scratch_cells(const Fftn& f);
 void fftn_pad(Fftn* f, const float2* modes, const float* const* dec, float2* grid,
               int nv, bool inv, cudaStream_t st, const GridHalo* halo = nullptr,
               const uint8_t* need = nullptr);
+// The same for a halo grid of which only the nx canonical planes of
+// dimension 0 in xlist (xmap: fine plane -> index in xlist, or -1) and the
+// stored planes marked in need are wanted: the X pass first, then Y and Z
+// over those planes only.  False (nothing launched) when the scratch planes
+// do not fit.
+bool fftn_pad_slab(Fftn* f, const float2* modes, const float* const* dec, float2* grid,
+                   int nv, bool inv, cudaStream_t st, const GridHalo& h,
+                   const uint8_t* need, const int* xmap, const int* xlist, int nx);
 // nv fine grids -> nv mode boxes of the transform times dec[d]; the grids are
 // overwritten (used as scratch)
 void fftn_crop(Fftn* f, float2* grid, const float* const* dec, float2* modes, int nv,

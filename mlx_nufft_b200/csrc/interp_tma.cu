@@ -38,12 +38,15 @@ namespace {
 
 constexpr int kSpinLimit = 1 << 22;
 
+// Threads per CTA of the 3-D TMA-staged interpolation and resident CTAs per
+// SM it is compiled for (80 registers): two 384-thread CTAs with two
+// 18 x 18 x 20-cell buffers each per SM (cfg-4 interp 5.29 ms vs 5.38 with
+// 256 threads).
 #ifndef NUFFT_TMA_MINB
-#define NUFFT_TMA_MINB 3
+#define NUFFT_TMA_MINB 2
 #endif
-// Threads per CTA of the 3-D TMA-staged interpolation.
 #ifndef NUFFT_TMA_THREADS
-#define NUFFT_TMA_THREADS 256
+#define NUFFT_TMA_THREADS 384
 #endif
 
 __host__ __device__ __forceinline__ int tma_buffer_cells(const TileGeom& tg, int B2) {

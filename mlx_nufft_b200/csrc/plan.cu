@@ -156,6 +156,12 @@ struct nufft_plan_s {
     // points); the stage API's grid is always written whole.
     uint8_t* xneed = nullptr;
     bool xneed_all = true;
+    // the interior planes among them (fine-grid x, in order) and the map
+    // x -> index in that list or -1 (device, n_up[0] ints each): the slab
+    // order of the pruned FFT computes only those planes
+    int* d_xlist = nullptr;
+    int* d_xmap = nullptr;
+    int nx_need = 0;
     std::map<int, cufftHandle> ffts;
     Fft1 fft1;                 // two-pass 1-D FFT (fft1.cu), when in use
     Fftn fftn;                 // pruned 3-D FFT with pad / crop (fft1.cu)
@@ -638,6 +644,24 @@ void setpts_t12(nufft_plan_s* p, int64_t M, const double* const* xs,
         NUFFT_CUDA(cudaMemcpyAsync(h.data(), p->xneed, P0, cudaMemcpyDeviceToHost, st));
         NUFFT_CUDA(cudaStreamSynchronize(st));
         for (int i = 0; i < P0; ++i) p->xneed_all &= h[i] != 0;
+        if (!p->xneed_all) {
+            const int n0 = (int)p->nup[0];
+            std::vector<int> list, map(n0, -1);
+            for (int x = 0; x < n0; ++x)
+                if (h[x + p->gh.lo[0]]) {
+                    map[x] = (int)list.size();
+                    list.push_back(x);
+                }
+            if (!p->d_xmap) {
+                p->d_xmap = (int*)dmalloc(sizeof(int) * n0, "plane map");
+                p->d_xlist = (int*)dmalloc(sizeof(int) * n0, "plane list");
+            }
+            NUFFT_CUDA(cudaMemcpy(p->d_xmap, map.data(), sizeof(int) * n0,
+                                  cudaMemcpyHostToDevice));
+            NUFFT_CUDA(cudaMemcpy(p->d_xlist, list.data(), sizeof(int) * list.size(),
+                                  cudaMemcpyHostToDevice));
+            p->nx_need = (int)list.size();
+        }
     }
     p->points_set = true;
 }
@@ -973,9 +997,16 @@ void execute_chunk(nufft_plan_s* p, const float2* in, float2* out, int nv,
                 fft1_rows(&p->fft1, p->gfft, 0, nullptr, nv, inv, st);
             } else if (use_fftn(p)) {  // pruned FFT with the pad fused
                 record(p, 1, st);
-                fftn_pad(&p->fftn, in, p->dec, p->gfft, nv, inv, st,
-                         p->halo ? &p->gh : nullptr,
-                         (stage == NUFFT_STAGE_ALL && !p->xneed_all) ? p->xneed : nullptr);
+                // an execute over a point set that reads only some planes:
+                // the slab order computes just those (NUFFT_FFTN_SLAB=0
+                // keeps the plain order and only skips their stores)
+                static const int slab_on = env_int("NUFFT_FFTN_SLAB", 1);
+                const bool pruned = stage == NUFFT_STAGE_ALL && p->halo && !p->xneed_all;
+                if (!(pruned && slab_on &&
+                      fftn_pad_slab(&p->fftn, in, p->dec, p->gfft, nv, inv, st, p->gh,
+                                    p->xneed, p->d_xmap, p->d_xlist, p->nx_need)))
+                    fftn_pad(&p->fftn, in, p->dec, p->gfft, nv, inv, st,
+                             p->halo ? &p->gh : nullptr, pruned ? p->xneed : nullptr);
             } else {
                 launch_pad(p->dim, p->N, p->nup, p->dec, in, p->gfft, p->fft64, nv,
                            st);
@@ -1441,6 +1472,8 @@ int nufft_plan_destroy(nufft_plan_t p) {
         dfree(p->gfft);
         dfree(p->gspread);
         dfree(p->xneed);
+        dfree(p->d_xmap);
+        dfree(p->d_xlist);
         dfree(p->d_ftd);
         dfree(p->d_fta);
         dfree(p->d_err);

@@ -280,11 +280,12 @@ def test_type2_3d_halo_grid(N, eps, isign, rng):
 def test_type2_3d_slab_points_pruned_planes(lo, hi, rng):
     """A 3-D type-2 plan whose points fill one slab of the first coordinate
     (as each rank's share in the x-slab split of bench.py): setpts marks the
-    grid planes its tiles read and the execute's last FFT pass writes only
-    those (plus their halo copies).  The first slab straddles the periodic
-    seam at 0 (tiles at both ends of the grid).  The execute equals the
-    staged execute (whose grid is written whole) bit for bit, and the fp64
-    restatement of the pipeline within the gate."""
+    grid planes its tiles read, and the execute computes only those (the
+    slab order of the pruned FFT: X pass first, then Y and Z over the marked
+    planes, plus their halo copies).  The first slab straddles the periodic
+    seam at 0 (tiles at both ends of the grid).  The execute matches the
+    staged execute (whose grid is the whole plain-order FFT) to FFT
+    rounding, and the fp64 restatement of the pipeline within the gate."""
     import torch
     from mlx_nufft_b200 import Type2PlanND, _lib
     N, P = (32, 32, 32), 100_000
@@ -300,5 +301,10 @@ def test_type2_3d_slab_points_pruned_planes(lo, hi, rng):
     plan._plan.execute_stage(_lib.STAGE_SPREAD, ft, None, 1)
     plan._plan.execute_stage(_lib.STAGE_FINISH, None, out, 1)
     torch.cuda.synchronize()
-    np.testing.assert_array_equal(got, out.cpu().numpy())
+    assert port.rel_l2(got, out.cpu().numpy()) <= 2e-6
     assert port.rel_l2(got, port.nufft_t2(x, fk, 1e-6, -1)) <= 2e-5
+    # and again with two vectors (one launch over both)
+    fks = np.stack([fk, (fk * (0.5 - 1j)).astype(np.complex64)])
+    gb = plan.execute_batch(fks)
+    assert port.rel_l2(gb[0], got) <= 1e-6
+    assert port.rel_l2(gb[1], port.nufft_t2(x, fks[1], 1e-6, -1)) <= 2e-5
