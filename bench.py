@@ -24,9 +24,11 @@ value, roofline, e2e and CPU baseline), `gpu_launches`, `clocks`.
 
 With N > 1 GPUs (torchrun) the workloads are partitioned, one process per
 GPU, strong scaling (the whole problem fixed): type 2 split by target (the
-points of each rank form one x-slab of the grid with 1/N of the points;
-every rank builds the fine grid itself -- `value` -- or rank 0 builds it
-and broadcasts it over NCCL -- the `broadcast` key), the batched type 1
+points of each rank form one x-slab of the grid, 3-D slabs of equal modelled
+cost -- points to interpolate plus grid planes to transform; every rank
+builds the planes of the fine grid its points read -- `value` -- or rank 0
+builds it whole and broadcasts it over NCCL -- the `broadcast` key), the
+batched type 1
 split by vector, type 1 split by point with an NCCL all-reduce of the fine
 grids, type 3 split by target and expi split by element.  Every partition
 reports the rel-L2 of its result against one GPU running the whole problem
@@ -831,13 +833,37 @@ def run_expi(ctx, cfg, k, steps, warmup, cpu, peak, peak_kind, unit, lo=None, hi
 
 
 # ------------------------------------------------------------ N GPUs
-def slab_split(x0, world, rank):
+# Per-rank cost model of the x-slab split of the 3-D type-2 workload (B200,
+# 512^3 grid, 12^3 interpolation bins): ~9.9e-8 ms per point interpolated,
+# and ~3.0e-3 ms per fine-grid plane the slab spans -- the slab-order FFT
+# beyond its first pass and the per-subproblem overhead (tile copy,
+# barrier) of the ~154 bins per plane that uniformly spread points occupy.
+# Fitted to the per-rank step times of a 4-GPU run split by point count
+# (9.3e6 points over 203 planes: 1.64 ms; 1.57e7 over 79 planes: 1.81-1.97
+# ms, each with ~0.1 ms of fixed cost).
+SLAB_MS_PER_POINT = 9.9e-8
+SLAB_MS_PER_PLANE = 3.0e-3
+
+
+def slab_split(x0, world, rank, n_planes=None):
     """Boolean mask of the points of `rank` when the points are split into
-    `world` slabs of the first coordinate holding equal counts (so each
-    rank's points touch one slab of the fine grid)."""
+    `world` slabs of the first coordinate (so each rank's points touch one
+    slab of the fine grid).  Without n_planes the slabs hold equal point
+    counts; with it (the fine grid's extent in that coordinate) they hold
+    equal modelled cost, interpolation per point plus the slab-order FFT per
+    grid plane the slab spans, so dense slabs are narrower."""
     if world == 1:
         return np.ones(x0.size, dtype=bool)
-    qs = np.quantile(x0, np.linspace(0.0, 1.0, world + 1)[1:-1])
+    if n_planes is None:
+        qs = np.quantile(x0, np.linspace(0.0, 1.0, world + 1)[1:-1])
+    else:
+        xs = np.sort(np.asarray(x0, dtype=np.float64))
+        # cumulative cost at each sorted point: points so far, and planes
+        # from -pi up to it
+        cum = (SLAB_MS_PER_POINT * np.arange(1, xs.size + 1)
+               + SLAB_MS_PER_PLANE * (xs + np.pi) * (n_planes / (2 * np.pi)))
+        targets = cum[-1] * np.arange(1, world) / world
+        qs = xs[np.minimum(np.searchsorted(cum, targets), xs.size - 1)]
     lo = -np.inf if rank == 0 else qs[rank - 1]
     hi = np.inf if rank == world - 1 else qs[rank]
     return (x0 >= lo) & (x0 < hi)
@@ -873,8 +899,14 @@ def run_split(ctx, gen, k, steps, warmup, headline, scale):
         return r
     launches = 0
     if cfg["type"] == 2:
-        # split by target: x-slabs of equal point counts
-        mask = slab_split(cfg["x"][0], W, R)
+        # split by target: x-slabs of equal modelled cost (points to
+        # interpolate, fine-grid planes to transform)
+        n_up0 = None
+        if len(cfg["x"]) == 3:               # the plan's n_up rule (sigma 2)
+            from mlx_nufft_b200 import sizing
+            w, _ = sizing.kernel_params(cfg["eps"], 2.0)
+            n_up0 = sizing.next235even(max(2 * w, int(np.ceil(2.0 * cfg["n_modes"][0]))))
+        mask = slab_split(cfg["x"][0], W, R, n_up0)
         xl = [v[mask] for v in cfg["x"]]
         plan = build_plan(cfg, x=xl)
         native = plan._plan
@@ -891,6 +923,12 @@ def run_split(ctx, gen, k, steps, warmup, headline, scale):
         launches = int(native.info().kernel_launches) - l0
         units = int(cfg["x"][0].size)
         stage_ms = stage_split(ctx, native, step, max(1, min(steps, 10)))
+        # every rank's own time per step and share of the split (the
+        # partition's balance; `value` takes the slowest rank)
+        ranks = gather_small(ctx, {"ms_per_step": float(np.mean(per)),
+                                   "points": int(info.M),
+                                   "x_range": [float(xl[0].min()), float(xl[0].max())]})
+        res["ranks"] = ranks
         # variant: rank 0 builds the grid, NCCL broadcast, every rank interps
         grid = par.plan_grid_storage(native)          # stored layout, halo included
         gview = torch.view_as_real(grid)
@@ -931,9 +969,10 @@ def run_split(ctx, gen, k, steps, warmup, headline, scale):
             ref = build_plan(cfg, x=xs).execute(data)
             got = np.concatenate([p[1] for p in allp])
             chk = float(np.linalg.norm(got - ref) / np.linalg.norm(ref))
-        res["partition"] = ("type 2 split by target: x-slab of equal point count "
-                            "per rank, fine grid built on every rank (value) or "
-                            "broadcast from rank 0 (broadcast)")
+        res["partition"] = ("type 2 split by target: x-slabs of equal modelled cost "
+                            "(points + fine-grid planes) per rank, fine grid built on "
+                            "every rank for its planes (value) or broadcast whole "
+                            "from rank 0 (broadcast)")
         ckeys = config_keys(cfg, k, info, W, rank_points=int(info.M))
         n_out = int(info.M)
         h2d = int(data.numel() * 8)

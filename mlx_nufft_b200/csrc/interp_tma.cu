@@ -40,8 +40,8 @@ constexpr int kSpinLimit = 1 << 22;
 
 // Threads per CTA of the 3-D TMA-staged interpolation and resident CTAs per
 // SM it is compiled for (80 registers): two 384-thread CTAs with two
-// 18 x 18 x 20-cell buffers each per SM (cfg-4 interp 5.29 ms vs 5.38 with
-// 256 threads).
+// 18 x 18 x 20-cell buffers each per SM (3-D type 2, 256^3 modes, 5e7
+// clustered points: interp 5.29 ms vs 5.38 with 256 threads).
 #ifndef NUFFT_TMA_MINB
 #define NUFFT_TMA_MINB 2
 #endif

@@ -280,8 +280,9 @@ void plane_tap_order(TileGeom& tg, int w) {
 // type 2 at 5e7 clustered points and 3-D type 3 at 1e6 -> 1e6).  The
 // TMA-staged complex64 interpolation at w <= 7 takes 12^3 bins (`m3i`):
 // two 18 x 18 x 20-cell buffers per CTA still fit two CTAs per SM, and the
-// larger subproblems even out the bank residues of their points (cfg 4
-// interp 5.37 ms vs 5.67 at 10^3, 5.79 at 11^3, 8.44 at 9^3).
+// larger subproblems even out the bank residues of their points (3-D type
+// 2, 256^3 modes, 5e7 clustered points: interp 5.37 ms vs 5.67 at 10^3,
+// 5.79 at 11^3, 8.44 at 9^3).
 bool halo_wanted(const nufft_plan_s* p);
 
 TileGeom make_tile(int dim, const int64_t* n, int w, double beta, int keval,
