@@ -834,15 +834,14 @@ def run_expi(ctx, cfg, k, steps, warmup, cpu, peak, peak_kind, unit, lo=None, hi
 
 # ------------------------------------------------------------ N GPUs
 # Per-rank cost model of the x-slab split of the 3-D type-2 workload (B200,
-# 512^3 grid, 12^3 interpolation bins): ~9.9e-8 ms per point interpolated,
-# and ~3.0e-3 ms per fine-grid plane the slab spans -- the slab-order FFT
+# 512^3 grid, 12^3 interpolation bins): ~9.0e-8 ms per point interpolated,
+# and ~2.2e-3 ms per fine-grid plane the slab spans -- the slab-order FFT
 # beyond its first pass and the per-subproblem overhead (tile copy,
 # barrier) of the ~154 bins per plane that uniformly spread points occupy.
-# Fitted to the per-rank step times of a 4-GPU run split by point count
-# (9.3e6 points over 203 planes: 1.64 ms; 1.57e7 over 79 planes: 1.81-1.97
-# ms, each with ~0.1 ms of fixed cost).
-SLAB_MS_PER_POINT = 9.9e-8
-SLAB_MS_PER_PLANE = 3.0e-3
+# Least-squares fit (with a constant of ~0.34 ms per rank) to the per-rank
+# step times of 4- and 8-GPU runs.
+SLAB_MS_PER_POINT = 9.0e-8
+SLAB_MS_PER_PLANE = 2.2e-3
 
 
 def slab_split(x0, world, rank, n_planes=None):

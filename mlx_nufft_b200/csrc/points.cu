@@ -183,20 +183,35 @@ __global__ void k_sub_count(const uint32_t* count, int64_t nbins, int msub,
     nsubs[b] = (count[b] + (uint32_t)msub - 1u) / (uint32_t)msub;
 }
 
+// Full (msub-point) and partial subproblems of each sort key.
+__global__ void k_sub_split(const uint32_t* count, int64_t nbins, int msub,
+                            uint32_t* nfull, uint32_t* npart) {
+    int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (b >= nbins) return;
+    nfull[b] = count[b] / (uint32_t)msub;
+    npart[b] = (count[b] % (uint32_t)msub) != 0u ? 1u : 0u;
+}
+
 // Subproblem table: one entry per <= msub points of a sort key; the entry
-// carries the spatial bin (key mod the number of spatial bins).
+// carries the spatial bin (key mod the number of spatial bins).  The full
+// subproblems come first (in key order, at fullofs[b]), then the partial
+// ones (at *nfull_total + partofs[b]): the persistent kernels take
+// subproblems in table order, so the longest ones (a dense bin's msub-point
+// pieces) start early instead of running alone at the end of a launch.
 __global__ void k_sub_fill(const uint32_t* count, const uint32_t* start,
-                           const uint32_t* subofs, int64_t nbins,
+                           const uint32_t* fullofs, const uint32_t* partofs,
+                           const uint32_t* nfull_total, int64_t nbins,
                            int64_t nbins_spatial, int msub, int4* subs) {
     int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (b >= nbins) return;
-    uint32_t n = count[b];
-    uint32_t k0 = subofs[b];
+    const uint32_t n = count[b];
+    const uint32_t nf = n / (uint32_t)msub;
     const int spatial = (int)(b % nbins_spatial);
     for (uint32_t k = 0; k * (uint32_t)msub < n; ++k) {
-        uint32_t s = start[b] + k * (uint32_t)msub;
-        uint32_t c = min((uint32_t)msub, n - k * (uint32_t)msub);
-        subs[k0 + k] = make_int4((int)s, (int)c, spatial, 0);
+        const uint32_t s = start[b] + k * (uint32_t)msub;
+        const uint32_t c = min((uint32_t)msub, n - k * (uint32_t)msub);
+        const uint32_t pos = k < nf ? fullofs[b] + k : *nfull_total + partofs[b];
+        subs[pos] = make_int4((int)s, (int)c, spatial, 0);
     }
 }
 
@@ -645,7 +660,7 @@ void build_impl(PointSet* ps, const CellParams& cp, int64_t M,
         // the scan total; one allocation kept in the point set
         auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
         const size_t pb = al(4 * (size_t)M), kb = al(4 * (size_t)(nbins + 1));
-        const size_t need = 2 * pb + 4 * kb + 256;
+        const size_t need = 2 * pb + 6 * kb + 256;
         if (need > ps->scratch_bytes) {
             dfree(ps->scratch);       // previous setpts synchronised its stream
             ps->scratch = nullptr;
@@ -660,7 +675,9 @@ void build_impl(PointSet* ps, const CellParams& cp, int64_t M,
         uint32_t* start = (uint32_t*)(sp + 2 * pb + kb);
         uint32_t* nsubs = (uint32_t*)(sp + 2 * pb + 2 * kb);
         uint32_t* subofs = (uint32_t*)(sp + 2 * pb + 3 * kb);
-        uint32_t* tot = (uint32_t*)(sp + 2 * pb + 4 * kb);
+        uint32_t* npart = (uint32_t*)(sp + 2 * pb + 4 * kb);
+        uint32_t* partofs = (uint32_t*)(sp + 2 * pb + 5 * kb);
+        uint32_t* tot = (uint32_t*)(sp + 2 * pb + 6 * kb);   // [0] subproblems, [1] full ones
         NUFFT_CUDA(cudaMemsetAsync(count, 0, 4 * (nbins + 1), st));
         k_bin_count<DIM><<<(unsigned)grid, bs, 0, st>>>(M, X, cp, key_of,
                                                        rank_of, count, d_err);
@@ -689,7 +706,15 @@ void build_impl(PointSet* ps, const CellParams& cp, int64_t M,
                                           "subproblems");
                 ps->subcap = std::max<int64_t>(h_tot, 1);
             }
-            k_sub_fill<<<gb, 256, 0, st>>>(count, start, subofs, nbins,
+            // full subproblems first: offsets of full and partial ones
+            // (nsubs / subofs reused for the full counts and offsets)
+            k_sub_split<<<gb, 256, 0, st>>>(count, nbins, msub, nsubs, npart);
+            NUFFT_LAUNCH("k_sub_split");
+            k_scan<<<1, 1024, 0, st>>>(nsubs, subofs, nbins, tot + 1);
+            NUFFT_LAUNCH("k_scan");
+            k_scan<<<1, 1024, 0, st>>>(npart, partofs, nbins, tot + 2);
+            NUFFT_LAUNCH("k_scan");
+            k_sub_fill<<<gb, 256, 0, st>>>(count, start, subofs, partofs, tot + 1, nbins,
                                            nbins_sp, msub, ps->subs);
             NUFFT_LAUNCH("k_sub_fill");
             ps->nsub = h_tot;

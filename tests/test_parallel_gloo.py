@@ -225,3 +225,41 @@ def test_batch_split_by_vector():
     assert res[0][:2] == (0, 3) and res[1][:2] == (3, 5)
     for r in (0, 1):
         assert port.rel_l2(res[r][2], ref) <= TOL
+
+
+def test_bench_slab_split_partitions_and_balances(monkeypatch):
+    """bench.py's x-slab split of a 3-D type-2 point set: the N masks cover
+    every point exactly once, and with the grid extent given the modelled
+    per-rank cost (points plus spanned planes) is equal across ranks and no
+    higher at its maximum than the equal-count split's, whose wide uniform
+    slabs are dearer."""
+    import importlib.util
+    import os
+    spec = importlib.util.spec_from_file_location(
+        "bench_mod", os.path.join(os.path.dirname(__file__), "..", "bench.py"))
+    b = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(b)
+    rng = np.random.default_rng(3)
+    M = 400_000
+    x0 = np.concatenate([rng.uniform(-np.pi, np.pi, M // 2),
+                         np.mod(rng.normal(0, 0.3, M // 2) + np.pi, 2 * np.pi) - np.pi])
+    # the per-point constant is for the 5e7-point workload: scale it to the
+    # sample so that the split sees the same trade-off
+    monkeypatch.setattr(b, "SLAB_MS_PER_POINT", b.SLAB_MS_PER_POINT * 5e7 / M)
+
+    def costs(n_planes, W):
+        out, seen = [], np.zeros(M, dtype=int)
+        for r in range(W):
+            m = b.slab_split(x0, W, r, n_planes)
+            seen += m
+            xs = x0[m]
+            width = (xs.max() - xs.min()) * 512 / (2 * np.pi)
+            out.append(b.SLAB_MS_PER_POINT * m.sum() + b.SLAB_MS_PER_PLANE * width)
+        assert np.all(seen == 1)
+        return np.array(out)
+
+    for W in (2, 4, 8):
+        bal, eq = costs(512, W), costs(None, W)
+        assert bal.max() <= eq.max() * 1.001
+        assert bal.max() - bal.min() <= 0.02 * bal.mean()
+    assert costs(None, 8).max() > 1.1 * costs(512, 8).max()
