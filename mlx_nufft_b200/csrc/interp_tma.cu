@@ -48,6 +48,11 @@ constexpr int kSpinLimit = 1 << 22;
 #ifndef NUFFT_TMA_THREADS
 #define NUFFT_TMA_THREADS 384
 #endif
+// Points per thread per round of the 3-D TMA-staged interpolation (their
+// global loads are issued together).
+#ifndef NUFFT_TMA_U
+#define NUFFT_TMA_U 2
+#endif
 
 __host__ __device__ __forceinline__ int tma_buffer_cells(const TileGeom& tg, int B2) {
     return ((tg.T[0] * tg.T[1] * B2) + 15) & ~15;
@@ -201,7 +206,7 @@ k_interp_tma(const __grid_constant__ CUtensorMap tmap, const float2* __restrict_
     __shared__ __align__(8) uint64_t bar[2];
     __shared__ int ring[2];
     __shared__ int s_tma;                                // 0: all tiles by hand
-    constexpr int U = 2;
+    constexpr int U = NUFFT_TMA_U;
     const int S = B2, PS = tg.T[1] * B2;
     // cells per vector buffer, rounded to 16 cells: every TMA destination
     // is 128-byte aligned

@@ -209,9 +209,10 @@ int env_int(const char* name, int dflt) {
 // Points per interpolation subproblem: 1-D subproblems are streamed
 // through a shared-memory stage (interp_tma.cu), at most kStreamMsubMax.
 int interp_msub(int dim) {
-    static const int m1 = env_int("NUFFT_MSUB_1D", 0);   // tuning override
+    static const int m1 = env_int("NUFFT_MSUB_1D", 0);   // tuning overrides
+    static const int mn = env_int("NUFFT_MSUB_ND", 0);
     return dim == 1 ? (m1 > 0 ? std::min(m1, kStreamMsubMax) : kStreamMsubMax)
-                    : kMsubInterp;
+                    : (mn > 0 ? std::min(mn, kMsubInterp) : kMsubInterp);
 }
 
 // ----------------------------------------------------------------------
