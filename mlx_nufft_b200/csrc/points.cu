@@ -193,11 +193,14 @@ __global__ void k_sub_split(const uint32_t* count, int64_t nbins, int msub,
 }
 
 // Subproblem table: one entry per <= msub points of a sort key; the entry
-// carries the spatial bin (key mod the number of spatial bins).  The full
-// subproblems come first (in key order, at fullofs[b]), then the partial
-// ones (at *nfull_total + partofs[b]): the persistent kernels take
-// subproblems in table order, so the longest ones (a dense bin's msub-point
-// pieces) start early instead of running alone at the end of a launch.
+// carries the spatial bin (key mod the number of spatial bins).  With
+// partofs (interpolation point sets) the full subproblems come first (in
+// key order, at fullofs[b]), then the partial ones (at *nfull_total +
+// partofs[b]): the persistent kernels take subproblems in table order, so
+// the longest ones (a dense bin's msub-point pieces) start early instead of
+// running alone at the end of a launch.  Without it (spreading, whose tile
+// flushes of neighbouring bins share L2 lines) the table is in key order,
+// bin b's subproblems at fullofs[b] on.
 __global__ void k_sub_fill(const uint32_t* count, const uint32_t* start,
                            const uint32_t* fullofs, const uint32_t* partofs,
                            const uint32_t* nfull_total, int64_t nbins,
@@ -210,7 +213,8 @@ __global__ void k_sub_fill(const uint32_t* count, const uint32_t* start,
     for (uint32_t k = 0; k * (uint32_t)msub < n; ++k) {
         const uint32_t s = start[b] + k * (uint32_t)msub;
         const uint32_t c = min((uint32_t)msub, n - k * (uint32_t)msub);
-        const uint32_t pos = k < nf ? fullofs[b] + k : *nfull_total + partofs[b];
+        const uint32_t pos = (!partofs || k < nf) ? fullofs[b] + k
+                                                  : *nfull_total + partofs[b];
         subs[pos] = make_int4((int)s, (int)c, spatial, 0);
     }
 }
@@ -706,15 +710,19 @@ void build_impl(PointSet* ps, const CellParams& cp, int64_t M,
                                           "subproblems");
                 ps->subcap = std::max<int64_t>(h_tot, 1);
             }
-            // full subproblems first: offsets of full and partial ones
-            // (nsubs / subofs reused for the full counts and offsets)
-            k_sub_split<<<gb, 256, 0, st>>>(count, nbins, msub, nsubs, npart);
-            NUFFT_LAUNCH("k_sub_split");
-            k_scan<<<1, 1024, 0, st>>>(nsubs, subofs, nbins, tot + 1);
-            NUFFT_LAUNCH("k_scan");
-            k_scan<<<1, 1024, 0, st>>>(npart, partofs, nbins, tot + 2);
-            NUFFT_LAUNCH("k_scan");
-            k_sub_fill<<<gb, 256, 0, st>>>(count, start, subofs, partofs, tot + 1, nbins,
+            if (cell_order) {
+                // interpolation: full subproblems first; offsets of full and
+                // partial ones (nsubs / subofs reused for the full counts
+                // and offsets)
+                k_sub_split<<<gb, 256, 0, st>>>(count, nbins, msub, nsubs, npart);
+                NUFFT_LAUNCH("k_sub_split");
+                k_scan<<<1, 1024, 0, st>>>(nsubs, subofs, nbins, tot + 1);
+                NUFFT_LAUNCH("k_scan");
+                k_scan<<<1, 1024, 0, st>>>(npart, partofs, nbins, tot + 2);
+                NUFFT_LAUNCH("k_scan");
+            }
+            k_sub_fill<<<gb, 256, 0, st>>>(count, start, subofs,
+                                           cell_order ? partofs : nullptr, tot + 1, nbins,
                                            nbins_sp, msub, ps->subs);
             NUFFT_LAUNCH("k_sub_fill");
             ps->nsub = h_tot;

@@ -431,7 +431,9 @@ k_spread_planes(const float2* __restrict__ c, int64_t cstride,
         // The staging thread's global loads are issued early: cells,
         // permutation and phase of the next chunk before this chunk's taps,
         // its strengths (through the permutation) before the barrier that
-        // waits for the taps of the other warps.
+        // waits for the taps of the other warps.  With one vector (PF off)
+        // the next chunk's loads wait for its own staging: the registers
+        // they would hold across the taps cost the kernel a resident CTA.
         int2 pcl[3];
         int64_t psrc = 0;
         float2 pph = make_float2(1.0f, 0.0f);
@@ -444,19 +446,27 @@ k_spread_planes(const float2* __restrict__ c, int64_t cstride,
                 if (phase) pph = __ldg(phase + j);
             }
         };
-        fetch(0);
+        constexpr bool PF = NV >= 2;
+        if constexpr (PF) fetch(0);
         for (int q = threadIdx.x; q < NV * TS; q += blockDim.x)
             tile[q] = make_float2(0.0f, 0.0f);
         for (int c0 = 0; c0 < cnt; c0 += kPlaneChunk) {
             const int n = min(kPlaneChunk, cnt - c0);
             float2 pcv[NV];
-            if (threadIdx.x < n) {
+            if constexpr (PF) {
+                if (threadIdx.x < n) {
 #pragma unroll
-                for (int v = 0; v < NV; ++v) pcv[v] = __ldg(c + v * cstride + psrc);
+                    for (int v = 0; v < NV; ++v) pcv[v] = __ldg(c + v * cstride + psrc);
+                }
             }
             __syncthreads();      // tile zeroed / previous chunk consumed
             if (threadIdx.x < n) {
                 const int p = threadIdx.x;
+                if constexpr (!PF) {
+                    fetch(c0);
+#pragma unroll
+                    for (int v = 0; v < NV; ++v) pcv[v] = __ldg(c + v * cstride + psrc);
+                }
                 int l0[3];
                 bool ok = true;
                 float wt[3][W];
@@ -487,7 +497,7 @@ k_spread_planes(const float2* __restrict__ c, int64_t cstride,
                 for (int v = 0; v < NV; ++v) s_c[p][v] = phase ? cmul(pcv[v], pph) : pcv[v];
             }
             __syncthreads();
-            if (c0 + kPlaneChunk < cnt) fetch(c0 + kPlaneChunk);
+            if (PF && c0 + kPlaneChunk < cnt) fetch(c0 + kPlaneChunk);
             for (int p = 0; p < n; ++p) {
                 const int2 pos = s_pos[p];
                 const int l0z = pos.x;
